@@ -1,0 +1,75 @@
+/* Plain C ABI of libzipserv_b200.so (ctypes / cffi / cgo friendly).
+ *
+ * Every function returns a cudaError_t value as int (0 = success). Pointers
+ * named d_* are device pointers; `stream` is a cudaStream_t (NULL = legacy
+ * default stream). Nothing here synchronises the host or allocates device
+ * memory. Each entry point cites the reference interface it replaces
+ * (paths inside the reference project).
+ */
+#ifndef ZIPSERV_B200_H
+#define ZIPSERV_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library version: major*10000 + minor*100 + patch. */
+int zs_version(void);
+
+/* Host exponent-window analysis.
+ * Replaces kernel_benchmark/utils.h:189 analyzeExponentDistribution_BF16 (rule 0)
+ * and the selection rule of kernel_benchmark/zipserv_decode_attention_ext.cu:65-133 (rule 1). */
+int zs_analyze_exponents_host(const uint16_t* a, int64_t numel, int rule, int* top7);
+
+/* Host encoder (multi-threaded), byte-identical to csrc/L_API.cu:559
+ * InitBF16MatrixTripleBitmap_Reuse. Sizes: sm >= M*K + 16*#GT bytes,
+ * full >= M*K + 8*#GT elements, bitmaps #ST = M*K/64 each, st_counts 2*#ST,
+ * mt_off 2*#MT (#MT = M*K/1024), gt_off 2*(#GT+1); scalars4 receives
+ * {max_hf, max_full, total_hf, total_full}. Temp memory is allocated on the host.
+ * Returns 0, or cudaErrorInvalidValue / cudaErrorMemoryAllocation. */
+int zs_encode_host(const uint16_t* a, int M, int K, const int* top7, uint8_t* sm, uint16_t* full,
+                   uint64_t* b1, uint64_t* b2, uint64_t* b3, int* st_counts, int* mt_off, int* gt_off,
+                   int* scalars4);
+
+/* Device scratch needed by zs_analyze_exponents (bytes). */
+size_t zs_analyze_scratch_bytes(void);
+
+/* GPU exponent-window analysis; writes 7 ints to d_top7 (stream ordered).
+ * Replaces kernel_benchmark/zipserv_decode_attention_ext.cu:137 AnalyzeTopExponentsGPU
+ * (rule 1) and gives the host rule of kernel_benchmark/utils.h:189 on the GPU (rule 0).
+ * d_in must be 16-byte aligned. */
+int zs_analyze_exponents(void* stream, const uint16_t* d_in, int64_t numel, int rule, void* d_scratch,
+                         int* d_top7);
+
+/* Device scratch needed by zs_encode for an M x K matrix (bytes). */
+size_t zs_encode_scratch_bytes(int M, int K);
+
+/* GPU encoder, byte-identical to the reference host encoder given the same top7.
+ * Replaces csrc/L_API.cu:1355 InitBF16MatrixTripleBitmap_GPU. Output sizes as in
+ * zs_encode_host; d_scalars4 (device) receives {max_hf, max_full, total_hf, total_full}. */
+int zs_encode(void* stream, const uint16_t* d_in, int M, int K, const int* d_top7, uint8_t* d_sm,
+              uint16_t* d_full, uint64_t* d_b1, uint64_t* d_b2, uint64_t* d_b3, int* d_st_counts,
+              int* d_mt_off, int* d_gt_off, void* d_scratch, int* d_scalars4);
+
+/* Dense decode, row-major M x K bf16 output.
+ * Replaces csrc/L_API.cu:234 BF16TripleBitmap_Decompress_API. d_err (nullable)
+ * receives error bits (1 = a wait timed out, 2 = an offset was out of range). */
+int zs_decompress(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const uint64_t* d_b1,
+                  const uint64_t* d_b2, const uint64_t* d_b3, const int* d_mt_off, const int* d_gt_off,
+                  int max_hf, int max_full, int start_exp, uint16_t* d_out, int M, int K,
+                  unsigned* d_err);
+
+/* ZipGEMM: d_c[n*M + m] = sum_k W[m][k] * d_x[n*K + k] (bf16 in/out, fp32 accumulate).
+ * Replaces csrc/L_API.cu:119 BF16TripleBitmap_MM_API (split-K reduced in-kernel;
+ * split_k >= 1 is a lower bound on the K split). */
+int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const uint64_t* d_b1,
+               const uint64_t* d_b2, const uint64_t* d_b3, const int* d_mt_off, const int* d_gt_off,
+               int max_hf, int max_full, int start_exp, const uint16_t* d_x, uint16_t* d_c, int M, int N,
+               int K, int split_k, unsigned* d_err);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

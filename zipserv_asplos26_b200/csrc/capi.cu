@@ -1,0 +1,130 @@
+// C ABI (include/zipserv_b200.h) and the reference's GPU C++ ABI
+// (include/L_API.cuh, same mangled names as the reference build/L_API.cuh).
+#include <cstdlib>
+#include <new>
+#include <vector>
+
+#include "L_API.cuh"
+#include "zipserv_b200.h"
+#include "zs_host.h"
+#include "zs_internal.h"
+
+extern "C" int zs_version(void) { return 100; }
+
+extern "C" int zs_analyze_exponents_host(const uint16_t* a, int64_t numel, int rule, int* top7) {
+    if (!a || !top7 || numel <= 0 || (rule != 0 && rule != 1)) return cudaErrorInvalidValue;
+    zs::analyze_host(a, numel, rule, top7);
+    return cudaSuccess;
+}
+
+extern "C" int zs_encode_host(const uint16_t* a, int M, int K, const int* top7, uint8_t* sm, uint16_t* full,
+                              uint64_t* b1, uint64_t* b2, uint64_t* b3, int* st_counts, int* mt_off, int* gt_off,
+                              int* scalars4) {
+    if (!a || !top7 || !sm || !full || !b1 || !b2 || !b3 || !st_counts || !mt_off || !gt_off || !scalars4)
+        return cudaErrorInvalidValue;
+    if (M <= 0 || K <= 0 || (M % 64) || (K % 64)) return cudaErrorInvalidValue;
+    const size_t ngt = (size_t)(M / 64) * (K / 64);
+    uint8_t* tsm = (uint8_t*)malloc(ngt * (4096 + 15));
+    uint16_t* tfu = (uint16_t*)malloc(ngt * (4096 + 7) * 2);
+    std::vector<int> c1, c2, o1, o2;
+    try {
+        c1.resize(ngt + 1); c2.resize(ngt + 1); o1.resize(ngt + 1); o2.resize(ngt + 1);
+    } catch (const std::bad_alloc&) {
+        free(tsm); free(tfu);
+        return cudaErrorMemoryAllocation;
+    }
+    if (!tsm || !tfu) { free(tsm); free(tfu); return cudaErrorMemoryAllocation; }
+    int r = zs::encode_host(a, M, K, top7, sm, full, b1, b2, b3, st_counts, mt_off, gt_off, tsm, tfu, c1.data(),
+                            c2.data(), o1.data(), o2.data(), &scalars4[0], &scalars4[1], &scalars4[2],
+                            &scalars4[3]);
+    free(tsm);
+    free(tfu);
+    return r < 0 ? cudaErrorInvalidValue : cudaSuccess;
+}
+
+extern "C" size_t zs_analyze_scratch_bytes(void) { return zs::kAnalyzeScratchBytes; }
+
+extern "C" int zs_analyze_exponents(void* stream, const uint16_t* d_in, int64_t numel, int rule, void* d_scratch,
+                                    int* d_top7) {
+    return zs::launch_analyze((cudaStream_t)stream, d_in, numel, rule, d_scratch, d_top7);
+}
+
+extern "C" size_t zs_encode_scratch_bytes(int M, int K) {
+    if (M <= 0 || K <= 0) return 0;
+    const size_t ngt = (size_t)(M / 64) * (K / 64);
+    return 4 * (ngt + 1) * sizeof(int) + 64;
+}
+
+extern "C" int zs_encode(void* stream, const uint16_t* d_in, int M, int K, const int* d_top7, uint8_t* d_sm,
+                         uint16_t* d_full, uint64_t* d_b1, uint64_t* d_b2, uint64_t* d_b3, int* d_st_counts,
+                         int* d_mt_off, int* d_gt_off, void* d_scratch, int* d_scalars4) {
+    if (!d_scratch || !d_scalars4 || M <= 0 || K <= 0) return cudaErrorInvalidValue;
+    const size_t ngt = (size_t)(M / 64) * (K / 64);
+    int* s = reinterpret_cast<int*>(d_scratch);
+    return zs::launch_encode((cudaStream_t)stream, d_in, M, K, d_top7, d_sm, d_full, d_b1, d_b2, d_b3,
+                             d_st_counts, d_mt_off, d_gt_off, s, s + (ngt + 1), s + 2 * (ngt + 1),
+                             s + 3 * (ngt + 1), d_scalars4, d_scalars4 + 1, d_scalars4 + 2, d_scalars4 + 3);
+}
+
+extern "C" int zs_decompress(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const uint64_t* d_b1,
+                             const uint64_t* d_b2, const uint64_t* d_b3, const int* d_mt_off, const int* d_gt_off,
+                             int max_hf, int max_full, int start_exp, uint16_t* d_out, int M, int K,
+                             unsigned* d_err) {
+    return zs::launch_decompress((cudaStream_t)stream, d_sm, d_full, d_b1, d_b2, d_b3, d_mt_off, d_gt_off, max_hf,
+                                 max_full, start_exp, d_out, M, K, d_err);
+}
+
+extern "C" int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const uint64_t* d_b1,
+                          const uint64_t* d_b2, const uint64_t* d_b3, const int* d_mt_off, const int* d_gt_off,
+                          int max_hf, int max_full, int start_exp, const uint16_t* d_x, uint16_t* d_c, int M,
+                          int N, int K, int split_k, unsigned* d_err) {
+    return zs::launch_zipgemm((cudaStream_t)stream, d_sm, d_full, d_b1, d_b2, d_b3, d_mt_off, d_gt_off, max_hf,
+                              max_full, start_exp, d_x, d_c, M, N, K, split_k, d_err);
+}
+
+// ---------------------- reference GPU ABI (C++ names) -----------------------
+cudaError_t BF16TripleBitmap_MM_API(cudaStream_t stream, const uint8_t* SignMantissa,
+                                    const __nv_bfloat16* CompressedFull, const uint64_t* Bitmap1,
+                                    const uint64_t* Bitmap2, const uint64_t* Bitmap3,
+                                    const int* TileOffsets_Median, const int* TileOffsets_Global,
+                                    const int max_high_freq_count, const int max_full_count,
+                                    const uint8_t start_exp, const __nv_bfloat16* B, __nv_bfloat16* C,
+                                    const int M_Global, const int N_Global, const int K_Global,
+                                    __nv_bfloat16* Reduction_Workspace, int Split_K) {
+    (void)Reduction_Workspace;
+    return zs::launch_zipgemm(stream, SignMantissa, reinterpret_cast<const uint16_t*>(CompressedFull), Bitmap1,
+                              Bitmap2, Bitmap3, TileOffsets_Median, TileOffsets_Global, max_high_freq_count,
+                              max_full_count, start_exp, reinterpret_cast<const uint16_t*>(B),
+                              reinterpret_cast<uint16_t*>(C), M_Global, N_Global, K_Global, Split_K, nullptr);
+}
+
+cudaError_t BF16TripleBitmap_Decompress_API(cudaStream_t stream, const uint8_t* SignMantissa,
+                                            const __nv_bfloat16* CompressedFull, const uint64_t* Bitmap1,
+                                            const uint64_t* Bitmap2, const uint64_t* Bitmap3,
+                                            const int* TileOffsets_Median, const int* TileOffsets_Global,
+                                            const int max_high_freq_count, const int max_full_count,
+                                            const uint8_t start_exp, __nv_bfloat16* Output, const int M_Global,
+                                            const int K_Global) {
+    return zs::launch_decompress(stream, SignMantissa, reinterpret_cast<const uint16_t*>(CompressedFull), Bitmap1,
+                                 Bitmap2, Bitmap3, TileOffsets_Median, TileOffsets_Global, max_high_freq_count,
+                                 max_full_count, start_exp, reinterpret_cast<uint16_t*>(Output), M_Global, K_Global,
+                                 nullptr);
+}
+
+cudaError_t InitBF16MatrixTripleBitmap_GPU(cudaStream_t stream, const __nv_bfloat16* d_input, int M, int K,
+                                           const int* d_top_exponents, uint8_t* d_sign_mantissa,
+                                           __nv_bfloat16* d_compressed_full, uint64_t* d_bitmap1,
+                                           uint64_t* d_bitmap2, uint64_t* d_bitmap3, int* d_tile_offsets,
+                                           int* d_tile_offsets_median, int* d_tile_offsets_global,
+                                           uint8_t* d_temp_sm, __nv_bfloat16* d_temp_full, int* d_gt_hf_count,
+                                           int* d_gt_full_count, int* d_hf_offsets, int* d_full_offsets,
+                                           int* d_max_hf_count, int* d_max_full_count, int* d_total_hf,
+                                           int* d_total_full) {
+    (void)d_temp_sm;
+    (void)d_temp_full;
+    return zs::launch_encode(stream, reinterpret_cast<const uint16_t*>(d_input), M, K, d_top_exponents,
+                             d_sign_mantissa, reinterpret_cast<uint16_t*>(d_compressed_full), d_bitmap1, d_bitmap2,
+                             d_bitmap3, d_tile_offsets, d_tile_offsets_median, d_tile_offsets_global, d_gt_hf_count,
+                             d_gt_full_count, d_hf_offsets, d_full_offsets, d_max_hf_count, d_max_full_count,
+                             d_total_hf, d_total_full);
+}

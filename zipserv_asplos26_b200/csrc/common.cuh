@@ -1,0 +1,317 @@
+// Shared device/host helpers for the B200 (sm_100a) ZipServ kernels:
+// TCA-TBE format constants, mbarrier / bulk-copy / TMA / tcgen05 PTX wrappers
+// with bounded waits, and the branch-free small-tile row decoder.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace zs {
+
+// ---------------------------------------------------------------------------
+// Format constants (csrc/L_API.cu:559-771 tiling: 8x8 small tile (ST),
+// 16x64 median tile (MT), 64x64 global tile (GT)).
+// ---------------------------------------------------------------------------
+constexpr int kGT = 64;            // global tile edge
+constexpr int kSTPerGT = 64;       // small tiles per global tile
+constexpr int kMTPerGT = 4;        // median tiles per global tile
+constexpr int kSTPerMT = 16;       // small tiles per median tile
+constexpr int kHfPad = 16;         // per-GT sign/mantissa stream padding (bytes)
+constexpr int kFullPad = 8;        // per-GT fallback stream padding (elements)
+
+// Error codes written to the optional device error word by bounded waits.
+constexpr unsigned kErrWaitTimeout = 1u;
+constexpr unsigned kErrStreamOverflow = 2u;
+
+// Upper bound on any single mbarrier wait: 2 s of wall time measured with
+// %globaltimer. Real waits in these kernels last microseconds.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ----------------------------- mbarrier -----------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                     smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and records kErrWaitTimeout
+// in *err when err != nullptr) if the phase did not complete within the limit.
+// `abort_flag` (shared memory) lets one thread's timeout stop the others early.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err,
+                                          volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    unsigned long long t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63) == 63) {
+            if (abort_flag && *abort_flag) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                if (err) atomicOr(err, kErrWaitTimeout);
+                if (abort_flag) *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// ------------------------- bulk copies (TMA engine) ------------------------
+// 1-D bulk copy global -> shared (this CTA), completion counted on `bar`.
+// Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 2-D tiled TMA load (no multicast), coordinates {c0 (innermost), c1}.
+__device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ------------------------------- cluster -----------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t cta) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(cta));
+    return r;
+}
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// ------------------------------- tcgen05 -----------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (bf16 in, fp32 acc).
+__device__ __forceinline__ void umma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive on `bar` once all previously issued tcgen05.mma of this thread finish.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// UMMA shared-memory matrix descriptor for a K-major tile stored in the
+// canonical 128-byte-swizzle layout: rows of 128 bytes (64 bf16), 8-row groups
+// 1024 bytes apart, 16-byte chunk c of row r stored at chunk (c ^ (r & 7)).
+// Tile base must be 1024-byte aligned. (Bit layout: start>>4 [0,14),
+// LBO>>4 [16,30), SBO>>4 [32,46), version 1 at [46,48), layout 2 = 128B
+// swizzle at [61,64).)
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;       // SBO
+    d |= (uint64_t)1 << 46;                 // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                 // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// Branch-free TCA-TBE row decode.
+//
+// One call decodes one row (8 consecutive elements along K) of one 8x8 small
+// tile. Inputs are that row's bytes of the three code bitmaps (bit j = column
+// j), the stream offsets of the row's first high-frequency byte and first
+// fallback element, and two 8-byte exponent tables:
+//   thb[c] = ((start_exp + c) mod 256) >> 1        (bf16 high byte, minus sign)
+//   tlb[c] = ((start_exp + c) & 1) << 7            (bf16 low byte exponent bit)
+// The result is four 32-bit words = 8 bf16 in column order, i.e. exactly the
+// 16 bytes of the row segment.
+//
+// Work per row: the code nibbles X (nibble j = code of column j) come from a
+// 256-entry bit->nibble spread table; the prefix-popcount selector for the
+// packed sign/mantissa bytes is spread(indicator) * 0x11111110; everything else
+// is byte permutes (prmt) and 3-input logic ops.
+// ---------------------------------------------------------------------------
+struct DecodeTables {
+    uint32_t thb0, thb1, tlb0, tlb1;
+};
+
+__host__ __device__ inline DecodeTables make_decode_tables(int start_exp) {
+    DecodeTables t;
+    uint32_t hb[2] = {0, 0}, lb[2] = {0, 0};
+    for (int c = 0; c < 8; ++c) {
+        uint32_t e = (uint32_t)(start_exp + c) & 0xFFu;
+        hb[c >> 2] |= (e >> 1) << (8 * (c & 3));
+        lb[c >> 2] |= ((e & 1u) << 7) << (8 * (c & 3));
+    }
+    t.thb0 = hb[0]; t.thb1 = hb[1]; t.tlb0 = lb[0]; t.tlb1 = lb[1];
+    return t;
+}
+
+// spread8[b]: nibble j = bit j of b.
+__host__ __device__ inline uint32_t spread8_value(uint32_t b) {
+    uint32_t r = 0;
+    for (int j = 0; j < 8; ++j) r |= ((b >> j) & 1u) << (4 * j);
+    return r;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t lop_or_and(uint32_t a, uint32_t mask, uint32_t b) {
+    return (a & mask) | b;  // compiles to a single LOP3
+}
+
+// c1, c2, c3: clean bytes (0..255) of the three bitmaps for this row.
+// sm: shared sign/mantissa stream (byte-addressed, 4-byte aligned base, at
+// least 8 readable bytes past the last valid one); hf_off: offset of the row's
+// first hf byte. full: fallback stream (bf16 bits); full_off: first fallback.
+__device__ __forceinline__ void decode_row(uint32_t c1, uint32_t c2, uint32_t c3, const uint32_t* spread,
+                                           const uint8_t* sm, uint32_t hf_off, const uint16_t* full,
+                                           uint32_t full_off, const DecodeTables& t, uint32_t (&o)[4]) {
+    const uint32_t ind = c1 | c2 | c3;
+    const uint32_t X = spread[c1] + (spread[c2] << 1) + (spread[c3] << 2);  // code nibbles
+    const uint32_t sel = spread[ind] * 0x11111110u;                          // hf-before-j nibbles
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(sm + (hf_off & ~3u));
+    const uint32_t sh = (hf_off & 3u) * 8u;
+    const uint32_t q0 = w[0], q1 = w[1], q2 = w[2];
+    const uint32_t lo = __funnelshift_r(q0, q1, sh);
+    const uint32_t hi = __funnelshift_r(q1, q2, sh);
+    const uint32_t s_lo = prmt(lo, hi, sel);
+    const uint32_t s_hi = prmt(lo, hi, sel >> 16);
+    const uint32_t hb_lo = lop_or_and(s_lo, 0x80808080u, prmt(t.thb0, t.thb1, X));
+    const uint32_t hb_hi = lop_or_and(s_hi, 0x80808080u, prmt(t.thb0, t.thb1, X >> 16));
+    const uint32_t lb_lo = lop_or_and(s_lo, 0x7F7F7F7Fu, prmt(t.tlb0, t.tlb1, X));
+    const uint32_t lb_hi = lop_or_and(s_hi, 0x7F7F7F7Fu, prmt(t.tlb0, t.tlb1, X >> 16));
+    o[0] = prmt(lb_lo, hb_lo, 0x5140);
+    o[1] = prmt(lb_lo, hb_lo, 0x7362);
+    o[2] = prmt(lb_hi, hb_hi, 0x5140);
+    o[3] = prmt(lb_hi, hb_hi, 0x7362);
+    uint32_t fm = (~ind) & 0xFFu;
+    if (fm) {
+        const uint16_t* f = full + full_off;
+        do {
+            const uint32_t j = __ffs(fm) - 1;
+            fm &= fm - 1;
+            const uint32_t v = *f++;
+            const uint32_t hsh = (j & 1u) * 16u;
+            const uint32_t keep = ~(0xFFFFu << hsh);
+            const uint32_t ins = v << hsh;
+            const uint32_t p = j >> 1;
+            o[0] = (p == 0) ? ((o[0] & keep) | ins) : o[0];
+            o[1] = (p == 1) ? ((o[1] & keep) | ins) : o[1];
+            o[2] = (p == 2) ? ((o[2] & keep) | ins) : o[2];
+            o[3] = (p == 3) ? ((o[3] & keep) | ins) : o[3];
+        } while (fm);
+    }
+}
+
+}  // namespace zs
+
+// Host-side error helper: turn a CUDA error into a return code.
+#define ZS_RETURN_IF_ERR(expr)                      \
+    do {                                            \
+        cudaError_t _e = (expr);                    \
+        if (_e != cudaSuccess) return _e;           \
+    } while (0)

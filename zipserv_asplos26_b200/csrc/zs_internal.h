@@ -1,0 +1,37 @@
+// Internal launchers shared between the .cu translation units of the library.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace zs {
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Exponent-window rules.
+//   0 = host rule (kernel_benchmark/utils.h:189 analyzeExponentDistribution_BF16)
+//   1 = torch-extension rule (kernel_benchmark/zipserv_decode_attention_ext.cu:35)
+enum WindowRule : int { kRuleHost = 0, kRuleExt = 1 };
+
+// Scratch for launch_analyze: 256 x u64 counters + 1 u32 ticket (2056 bytes).
+constexpr size_t kAnalyzeScratchBytes = 256 * 8 + 8;
+
+cudaError_t launch_analyze(cudaStream_t s, const uint16_t* in, long long numel, int rule, void* scratch,
+                           int* d_top);
+
+// Per-GT scratch for launch_encode: 4 x (#GT + 1) ints.
+cudaError_t launch_encode(cudaStream_t s, const uint16_t* in, int M, int K, const int* d_top, uint8_t* sm,
+                          uint16_t* full, uint64_t* b1, uint64_t* b2, uint64_t* b3, int* st_counts,
+                          int* mt_off, int* gt_off, int* gt_hf_cnt, int* gt_full_cnt, int* hf_prefix,
+                          int* full_prefix, int* d_max_hf, int* d_max_full, int* d_total_hf, int* d_total_full);
+
+cudaError_t launch_decompress(cudaStream_t s, const uint8_t* sm, const uint16_t* full, const uint64_t* b1,
+                              const uint64_t* b2, const uint64_t* b3, const int* mt_off, const int* gt_off,
+                              int max_hf, int max_full, int start_exp, uint16_t* out, int M, int K,
+                              unsigned* err);
+
+cudaError_t launch_zipgemm(cudaStream_t s, const uint8_t* sm, const uint16_t* full, const uint64_t* b1,
+                           const uint64_t* b2, const uint64_t* b3, const int* mt_off, const int* gt_off,
+                           int max_hf, int max_full, int start_exp, const uint16_t* X, uint16_t* C, int M,
+                           int N, int K, int split_k, unsigned* err);
+
+}  // namespace zs
