@@ -28,6 +28,7 @@ constexpr unsigned kErrStreamOverflow = 2u;
 // Upper bound on any single mbarrier wait: 2 s of wall time measured with
 // %globaltimer. Real waits in these kernels last microseconds.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
@@ -60,14 +61,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// One potentially blocking test of an mbarrier phase. The suspend-time hint
+// lets the hardware park the waiting thread (up to ~1 ms) until the phase
+// completes, so waiting warps do not spin and steal issue slots from the
+// decoders sharing the SM.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
         : "memory");
     return ok != 0;
 }
@@ -78,12 +83,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err,
                                           volatile int* abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
-    unsigned long long t0 = globaltimer_ns();
+    // Deadline on the SM cycle counter (cheap to read, unlike %globaltimer):
+    // kWaitLimitCycles is ~2 s at B200 clocks.
+    const long long t0 = clock64();
     for (uint32_t it = 0;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63) == 63) {
             if (abort_flag && *abort_flag) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (clock64() - t0 > kWaitLimitCycles) {
                 if (err) atomicOr(err, kErrWaitTimeout);
                 if (abort_flag) *abort_flag = 1;
                 return false;
@@ -175,6 +182,24 @@ __device__ __forceinline__ void umma_bf16_ss(uint32_t d_tmem, uint64_t adesc, ui
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16. A (M=128 x K=16 bf16) is in
+// TMEM: row m in lane m, K packed two bf16 per 32-bit column (8 columns).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// This warp's 32 lanes each write 4 consecutive 32-bit columns of their own
+// TMEM lane (lane quarter = warp % 4).
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Arrive on `bar` once all previously issued tcgen05.mma of this thread finish.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -253,6 +278,38 @@ __host__ __device__ inline uint32_t spread8_value(uint32_t b) {
     return r;
 }
 
+// Shared-memory accesses on 32-bit shared addresses. The loads carry no memory
+// clobber, so the compiler may overlap them with the stores of earlier rows;
+// callers pass addresses derived through launder() after the barrier that
+// makes the data valid (launder is volatile, so it cannot move above the wait,
+// and every load depends on it).
+__device__ __forceinline__ uint32_t launder(uint32_t a) {
+    uint32_t r;
+    asm volatile("mov.b32 %0, %1;" : "=r"(r) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short v;
+    asm("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ void sts16(uint32_t a, uint32_t v) {
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"((unsigned short)v) : "memory");
+}
+
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
     uint32_t d;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
@@ -263,19 +320,36 @@ __device__ __forceinline__ uint32_t lop_or_and(uint32_t a, uint32_t mask, uint32
     return (a & mask) | b;  // compiles to a single LOP3
 }
 
-// c1, c2, c3: clean bytes (0..255) of the three bitmaps for this row.
-// sm: shared sign/mantissa stream (byte-addressed, 4-byte aligned base, at
-// least 8 readable bytes past the last valid one); hf_off: offset of the row's
-// first hf byte. full: fallback stream (bf16 bits); full_off: first fallback.
-__device__ __forceinline__ void decode_row(uint32_t c1, uint32_t c2, uint32_t c3, const uint32_t* spread,
-                                           const uint8_t* sm, uint32_t hf_off, const uint16_t* full,
-                                           uint32_t full_off, const DecodeTables& t, uint32_t (&o)[4]) {
-    const uint32_t ind = c1 | c2 | c3;
-    const uint32_t X = spread[c1] + (spread[c2] << 1) + (spread[c3] << 2);  // code nibbles
-    const uint32_t sel = spread[ind] * 0x11111110u;                          // hf-before-j nibbles
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(sm + (hf_off & ~3u));
-    const uint32_t sh = (hf_off & 3u) * 8u;
-    const uint32_t q0 = w[0], q1 = w[1], q2 = w[2];
+// Spread table in shared memory, one private copy per lane (bank): entry b of
+// lane l is the word at byte offset b * 128 + l * 4.
+constexpr int kLutCopies = 32;
+constexpr int kLutWords = 256 * kLutCopies;
+
+__device__ __forceinline__ uint32_t spread8_fast(uint32_t x) {
+    x = (x | (x << 12)) & 0x000F000Fu;
+    x = (x | (x << 6)) & 0x03030303u;
+    x = (x | (x << 3)) & 0x11111111u;
+    return x;
+}
+
+__device__ __forceinline__ void fill_spread_table(uint32_t* lut, int tid, int nthreads) {
+    for (int i = tid; i < kLutWords; i += nthreads) lut[i] = spread8_fast((uint32_t)(i / kLutCopies));
+}
+
+// Decode the high-frequency elements of one small-tile row (8 elements).
+// c1, c2, c3: clean bytes of the three bitmaps for this row. lut_lane: shared
+// address of this lane's table copy. win: shared address of the row's first hf
+// byte (the stream base is 16-byte aligned; >= 12 bytes readable from win & ~3).
+// Fallback positions (code 0) receive junk; the caller patches them.
+__device__ __forceinline__ void decode_row_hf(uint32_t c1, uint32_t c2, uint32_t c3, uint32_t lut_lane,
+                                              uint32_t win, const DecodeTables& t, uint32_t (&o)[4]) {
+    const uint32_t s1 = lds32(lut_lane + (c1 << 7)), s2 = lds32(lut_lane + (c2 << 7)),
+                   s3 = lds32(lut_lane + (c3 << 7));
+    const uint32_t X = s1 + (s2 << 1) + (s3 << 2);        // code nibbles
+    const uint32_t sel = (s1 | s2 | s3) * 0x11111110u;    // hf-before-j nibbles
+    const uint32_t wa = win & ~3u;
+    const uint32_t sh = (win & 3u) * 8u;
+    const uint32_t q0 = lds32(wa), q1 = lds32(wa + 4), q2 = lds32(wa + 8);
     const uint32_t lo = __funnelshift_r(q0, q1, sh);
     const uint32_t hi = __funnelshift_r(q1, q2, sh);
     const uint32_t s_lo = prmt(lo, hi, sel);
@@ -288,23 +362,6 @@ __device__ __forceinline__ void decode_row(uint32_t c1, uint32_t c2, uint32_t c3
     o[1] = prmt(lb_lo, hb_lo, 0x7362);
     o[2] = prmt(lb_hi, hb_hi, 0x5140);
     o[3] = prmt(lb_hi, hb_hi, 0x7362);
-    uint32_t fm = (~ind) & 0xFFu;
-    if (fm) {
-        const uint16_t* f = full + full_off;
-        do {
-            const uint32_t j = __ffs(fm) - 1;
-            fm &= fm - 1;
-            const uint32_t v = *f++;
-            const uint32_t hsh = (j & 1u) * 16u;
-            const uint32_t keep = ~(0xFFFFu << hsh);
-            const uint32_t ins = v << hsh;
-            const uint32_t p = j >> 1;
-            o[0] = (p == 0) ? ((o[0] & keep) | ins) : o[0];
-            o[1] = (p == 1) ? ((o[1] & keep) | ins) : o[1];
-            o[2] = (p == 2) ? ((o[2] & keep) | ins) : o[2];
-            o[3] = (p == 3) ? ((o[3] & keep) | ins) : o[3];
-        } while (fm);
-    }
 }
 
 }  // namespace zs

@@ -2,31 +2,36 @@
 // Replaces csrc/L_Kernel.cuh:1110 BF16TripleBitmap_Decompress_Kernel and
 // csrc/L_API.cu:234 BF16TripleBitmap_Decompress_API.
 //
-// One CTA (4 warps) per pair of 64x64 global tiles. Thread 0 pulls each GT's
-// five streams into shared memory with 1-D bulk copies (the GT's hf and
+// One CTA (8 warps) per group of four 64x64 global tiles. Thread 0 pulls each
+// GT's five streams into shared memory with 1-D bulk copies (the GT's hf and
 // fallback streams are contiguous and 16-byte aligned thanks to the format's
-// per-GT padding); each warp then decodes 32 rows with the branch-free row
-// decoder into a bank-swizzled 64x64 tile, and the CTA writes the tile out with
-// 16-byte coalesced stores (8 threads per 128-byte row).
+// per-GT padding); two warps per GT then decode 32 rows each with the
+// branch-free row decoder into a bank-swizzled 64x64 tile, and the CTA writes
+// the tiles out with 16-byte coalesced stores (8 threads per 128-byte row).
+// The decoder is latency bound per warp, so the CTA is kept small enough for
+// several to share an SM.
 #include "common.cuh"
 #include "tile_decode.cuh"
 #include "zs_internal.h"
 
 namespace zs {
 
+constexpr int kDecompGTs = 4;                     // global tiles per CTA
+constexpr int kDecompThreads = 64 * kDecompGTs;   // two warps per GT
+
 struct DecompSmemLayout {
     uint32_t lut, bar, gt_base, gt_stride, bm, mt, hfs, fulls, tile, total;
     __host__ __device__ DecompSmemLayout(int max_hf, int max_full) {
-        lut = 0;                          // 256 x u32 spread table
-        bar = 1024;                       // mbarrier
-        gt_base = 1040;
+        lut = 0;                          // replicated spread table
+        bar = 4 * kLutWords;              // mbarrier
+        gt_base = bar + 16;
         bm = 0;                           // 3 x 512 B
         mt = 1536;                        // 32 B
         hfs = 1568;                       // hf slot
         fulls = hfs + hf_slot_bytes(max_hf);
         tile = round_up_u32(fulls + full_slot_bytes(max_full), 16);
         gt_stride = round_up_u32(tile + 8192, 16);
-        total = gt_base + 2 * gt_stride;
+        total = gt_base + kDecompGTs * gt_stride;
     }
 };
 
@@ -42,7 +47,7 @@ __device__ __forceinline__ void issue_gt_copies(uint8_t* base, const DecompSmemL
     if (c.fb) bulk_g2s(base + L.fulls, full + c.f0, c.fb, bar);
 }
 
-__global__ void __launch_bounds__(128) decompress_kernel(const uint8_t* __restrict__ sm,
+__global__ void __launch_bounds__(kDecompThreads) decompress_kernel(const uint8_t* __restrict__ sm,
                                                          const uint16_t* __restrict__ full,
                                                          const uint64_t* __restrict__ b1,
                                                          const uint64_t* __restrict__ b2,
@@ -59,11 +64,10 @@ __global__ void __launch_bounds__(128) decompress_kernel(const uint8_t* __restri
     const int tid = threadIdx.x;
     const int gtk = K / kGT;
     const long long ngt = (long long)(M / kGT) * gtk;
-    const long long gt0 = 2ll * blockIdx.x;
-    const int nsub = (int)min(2ll, (long long)ngt - gt0);
+    const long long gt0 = (long long)kDecompGTs * blockIdx.x;
+    const int nsub = (int)min((long long)kDecompGTs, ngt - gt0);
 
-    lut[tid] = spread8_value(tid);
-    lut[tid + 128] = spread8_value(tid + 128);
+    fill_spread_table(lut, tid, kDecompThreads);
     if (tid == 0) {
         abort_flag = 0;
         mbar_init(bar, 1);
@@ -71,7 +75,7 @@ __global__ void __launch_bounds__(128) decompress_kernel(const uint8_t* __restri
     }
     __syncthreads();
     if (tid == 0) {
-        GtCopy c[2];
+        GtCopy c[kDecompGTs];
         uint32_t total = 0;
         for (int s = 0; s < nsub; ++s) {
             c[s] = gt_copy_range(gt_off, gt0 + s, max_hf, max_full, err);
@@ -88,24 +92,24 @@ __global__ void __launch_bounds__(128) decompress_kernel(const uint8_t* __restri
     const int sub = warp >> 1;
     const DecodeTables tabs = make_decode_tables(start_exp);
     if (ok && sub < nsub) {
-        uint8_t* base = smem + L.gt_base + sub * L.gt_stride;
-        GtSmem g;
-        g.bm1 = reinterpret_cast<const uint64_t*>(base + L.bm);
-        g.bm2 = g.bm1 + 64;
-        g.bm3 = g.bm1 + 128;
-        g.mt = reinterpret_cast<const int*>(base + L.mt);
+        const uint32_t base = launder(smem_u32(smem + L.gt_base + sub * L.gt_stride));
+        GtView g;
+        g.bm = base + L.bm;
+        g.bstride = 512;
+        g.mt = base + L.mt;
         g.sm = base + L.hfs;
-        g.full = reinterpret_cast<const uint16_t*>(base + L.fulls);
+        g.full = base + L.fulls;
         g.hf_cap = hf_slot_bytes(max_hf) - 16;
         g.full_cap = full_slot_bytes(max_full) / 2 - 8;
-        uint8_t* tile = base + L.tile;
-        decode_gt_half(g, lut, tabs, warp & 1, [&](int m, int kc, const uint32_t(&o)[4]) {
-            *reinterpret_cast<uint4*>(tile + m * 128 + ((kc ^ (m & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-        });
+        const uint32_t lut_lane = launder(smem_u32(lut)) + 4u * (uint32_t)(tid & 31);
+        if (warp & 1)
+            decode_gt_rows<true, 8>(g, lut_lane, tabs, base + L.tile, 0);
+        else
+            decode_gt_rows<false, 8>(g, lut_lane, tabs, base + L.tile, 0);
     }
     __syncthreads();
     if (!ok) return;
-    for (int idx = tid; idx < nsub * 512; idx += 128) {
+    for (int idx = tid; idx < nsub * 512; idx += kDecompThreads) {
         const int s = idx >> 9, row = (idx >> 3) & 63, c = idx & 7;
         const long long gt = gt0 + s;
         const uint8_t* tile = smem + L.gt_base + s * L.gt_stride + L.tile;
@@ -131,8 +135,8 @@ cudaError_t launch_decompress(cudaStream_t stream, const uint8_t* sm, const uint
     const DecompSmemLayout L(max_hf, max_full);
     ZS_RETURN_IF_ERR(cudaFuncSetAttribute(decompress_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)L.total));
-    const long long grid = (ngt + 1) / 2;
-    decompress_kernel<<<(unsigned)grid, 128, L.total, stream>>>(sm, full, b1, b2, b3, mt_off, gt_off, max_hf,
+    const long long grid = (ngt + kDecompGTs - 1) / kDecompGTs;
+    decompress_kernel<<<(unsigned)grid, kDecompThreads, L.total, stream>>>(sm, full, b1, b2, b3, mt_off, gt_off, max_hf,
                                                                 max_full, start_exp & 0xFF, out, M, K, err);
     return cudaGetLastError();
 }

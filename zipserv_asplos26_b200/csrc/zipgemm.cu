@@ -8,23 +8,26 @@
 // C[n*M + m] = sum_k W[m][k] * X[n][k], fp32 accumulate, bf16 output.
 //
 // One CTA computes a 128-row x BN-column output tile over a range of K blocks
-// (64 columns each = one global tile column). Warp roles (320 threads):
-//   warp 8      producer: per K block, 1-D bulk copies of the two GTs' bitmaps,
-//               median offsets and hf / fallback streams, plus a 2-D TMA load
-//               of the 64 x BN activation tile (128-byte swizzle), all on one
-//               mbarrier with expect_tx.
-//   warps 0..7  decoders, two groups of four alternating K blocks. Lane = W row:
-//               each thread decodes its row's 8 column blocks with the
-//               branch-free row decoder and stores 16-byte chunks straight into
-//               the UMMA canonical K-major 128-byte-swizzled A tile.
-//   warp 9      TMEM allocator + MMA issuer: tcgen05.mma kind::f16
-//               (M=128, N=BN, K=16) x4 per K block, accumulator in TMEM;
-//               tcgen05.commit releases the stage.
+// (64 columns each = one global-tile (GT) column; a block holds two GTs).
+// Three shared-memory rings decouple the stages of the pipeline:
+//   compressed ring  per K block: both GTs' bitmaps, median offsets and hf /
+//                    fallback streams, pulled by 1-D bulk copies (warp kCompWarp)
+//   B ring           the 64 x BN activation tile, 2-D TMA with 128-byte swizzle
+//                    (warp kBWarp)
+//   A ring           the decoded 128 x 64 bf16 weight tile in the UMMA canonical
+//                    K-major 128-byte-swizzled layout (written by the decoders)
+// Decoders: kDecodeGroups groups of 8 warps, each group decoding every
+// kDecodeGroups-th K block. In a group, warp (kh, q) owns rows 32q..32q+31 and
+// column blocks 4kh..4kh+3; lane = weight row. The decoder is latency bound per
+// warp, so many warps are kept resident (one CTA per SM, 27 warps).
+// MMA: warp kMmaWarp owns TMEM and issues tcgen05.mma kind::f16 (M=128, N=BN,
+// K=16) x4 per K block, fp32 accumulator in TMEM; tcgen05.commit frees the A
+// and B slots.
 // Split-K: the K blocks are split over the CTAs of a thread-block cluster
-// (1 x S x 1). Each CTA drains its TMEM accumulator into its own shared memory,
-// and after a cluster barrier every CTA reduces a slice of the output columns
-// by reading all S partial tiles over distributed shared memory, then writes
-// bf16 with coalesced 8-byte stores. No global workspace, no second kernel.
+// (1 x S x 1). Each CTA drains its accumulator into its own shared memory, and
+// after a cluster barrier every CTA reduces a slice of the output columns by
+// reading all S partial tiles over distributed shared memory, then writes bf16
+// with coalesced 8-byte stores. No global workspace and no second kernel.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -36,11 +39,17 @@
 
 namespace zs {
 
-constexpr int kGemmThreads = 320;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr uint32_t kHeaderBytes = 2048;
-constexpr int kMaxStages = 8;
+constexpr int kDecodeGroups = 6;
+constexpr int kDecodeWarps = 4 * kDecodeGroups;
+constexpr int kCompWarp = kDecodeWarps;
+constexpr int kBWarp = kDecodeWarps + 1;
+constexpr int kMmaWarp = kDecodeWarps + 2;
+constexpr int kGemmThreads = 32 * (kDecodeWarps + 3);
+constexpr int kMaxRing = 12;
+constexpr uint32_t kLutOffset = 1024;
+constexpr uint32_t kOffsOffset = kLutOffset + 4u * kLutWords;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kASlotCols = 32;      // one decoded 128 x 64 bf16 A tile in TMEM
 
 struct GemmParams {
     const uint8_t* sm;
@@ -55,49 +64,86 @@ struct GemmParams {
     int M, N, K;
     int BN;            // output columns per CTA (multiple of 16, <= 256)
     int kb_per_split;  // K blocks per cluster rank
-    int nstages;
+    int nc, na, nb;    // ring depths
+    int chunk;         // K blocks per compressed-ring slot (one bulk copy per stream per GT row)
     uint32_t tmem_cols;
-    // stage layout (bytes)
-    uint32_t stage_bytes, off_b, off_bm, off_mt, off_hf, off_full, hf_slot, full_slot;
+    uint32_t off_b, off_c;          // smem ring bases (contiguous: B, compressed)
+    uint32_t a_col;                 // TMEM column of A slot 0 (slots are kASlotCols apart)
+    uint32_t b_slot, c_slot;        // smem slot sizes
+    // compressed slot = 2 GT rows x [b1 | b2 | b3 (512*chunk each) | mt (32*chunk) | hf | fallback]
+    uint32_t c_row, c_mt, c_hf, c_full;
+    uint32_t hf_cap, full_cap;      // bytes available for one row's hf / fallback streams of a chunk
     unsigned* err;
 };
 
 struct GemmHeader {
-    uint64_t full[kMaxStages];
-    uint64_t decoded[kMaxStages];
-    uint64_t empty[kMaxStages];
+    uint64_t comp_full[kMaxRing], comp_empty[kMaxRing];
+    uint64_t a_full[kMaxRing], a_empty[kMaxRing];
+    uint64_t b_full[kMaxRing], b_empty[kMaxRing];
     uint64_t accum;
     uint32_t tmem_base;
     int abort_flag;
 };
 
+#ifdef ZS_TRACE
+// Diagnostic build only (-DZS_TRACE): per-CTA %globaltimer stamps.
+__device__ unsigned long long* g_zs_trace = nullptr;
+#define ZS_STAMP(slot)                                                                                    \
+    do {                                                                                                  \
+        if (zs_trace_ptr && (slot) < 256) {                                                               \
+            const size_t cta_ = blockIdx.x + (size_t)gridDim.x * (blockIdx.y + (size_t)gridDim.y * blockIdx.z); \
+            zs_trace_ptr[cta_ * 256 + (slot)] = (unsigned long long)clock64();                                  \
+        }                                                                                                 \
+    } while (0)
+#else
+#define ZS_STAMP(slot) \
+    do {               \
+    } while (0)
+#endif
+
+__device__ __forceinline__ uint32_t ring_parity(int i, int n) { return (uint32_t)((i / n) & 1); }
+// parity of the previous use of slot i % n (i >= n)
+__device__ __forceinline__ uint32_t ring_prev_parity(int i, int n) { return (uint32_t)(((i / n) + 1) & 1); }
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     zipgemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint32_t* lut = reinterpret_cast<uint32_t*>(smem);
-    GemmHeader* hd = reinterpret_cast<GemmHeader*>(smem + 1024);
-    uint8_t* stages = smem + kHeaderBytes;
+#ifdef ZS_TRACE
+    unsigned long long* const zs_trace_ptr = g_zs_trace;
+#endif
+    GemmHeader* hd = reinterpret_cast<GemmHeader*>(smem);
+    uint32_t* lut = reinterpret_cast<uint32_t*>(smem + kLutOffset);
+    int2* offs = reinterpret_cast<int2*>(smem + kOffsOffset);   // [2][kb_per_split + 1]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mtile = blockIdx.x, ntile = blockIdx.z;
     const uint32_t rank = cluster_ctarank();
     const int S = gridDim.y;
-    const int nkb = p.K / kGT, gtk = nkb;
+    const int gtk = p.K / kGT;
     const int kb0 = (int)rank * p.kb_per_split;
-    const int nk = max(0, min(nkb, kb0 + p.kb_per_split) - kb0);
+    const int nk = max(0, min(gtk, kb0 + p.kb_per_split) - kb0);
     const int gm0 = 2 * mtile;                      // first GT row of this tile
     const bool has_g1 = (gm0 + 1) < (p.M / kGT);    // second GT row present
-    const int NS = p.nstages;
+    const int ostride = p.kb_per_split + 1;
 
-    for (int i = tid; i < 256; i += kGemmThreads) lut[i] = spread8_value(i);
+    // The producer warp stages the GT offsets first; the global-load latency
+    // overlaps the table fill and the TMEM allocation.
+    if (warp == kCompWarp) {
+        for (int sub = 0; sub < (has_g1 ? 2 : 1); ++sub) {
+            const int2* src = reinterpret_cast<const int2*>(p.gt_off) + (long long)(gm0 + sub) * gtk + kb0;
+            for (int i = lane; i <= nk; i += 32) offs[sub * ostride + i] = src[i];
+        }
+    }
+    fill_spread_table(lut, tid, kGemmThreads);
     if (tid == 0) {
         // the 128-byte-swizzled operand tiles need a 1024-byte aligned window
         if ((smem_u32(smem) & 1023u) && p.err) atomicOr(p.err, kErrStreamOverflow);
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&hd->full[s], 1);
-            mbar_init(&hd->decoded[s], 4);
-            mbar_init(&hd->empty[s], 1);
+        for (int s = 0; s < p.nc; ++s) {
+            mbar_init(&hd->comp_full[s], 1);
+            mbar_init(&hd->comp_empty[s], 4 * p.chunk);   // every K block of the chunk, 4 warps each
         }
+        for (int s = 0; s < p.na; ++s) { mbar_init(&hd->a_full[s], 4); mbar_init(&hd->a_empty[s], 1); }
+        for (int s = 0; s < p.nb; ++s) { mbar_init(&hd->b_full[s], 1); mbar_init(&hd->b_empty[s], 1); }
         mbar_init(&hd->accum, 1);
         hd->abort_flag = 0;
         fence_mbar_init();
@@ -106,100 +152,146 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_alloc(&hd->tmem_base, p.tmem_cols);
         tmem_relinquish();
     }
-    if (warp == kProducerWarp && lane == 0) prefetch_tmap(&tmap_x);
+    if (warp == kBWarp && lane == 0) prefetch_tmap(&tmap_x);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_d = hd->tmem_base;
     volatile int* abort_flag = &hd->abort_flag;
+    if (tid == 0) ZS_STAMP(0);
 
-    if (warp == kProducerWarp) {
+    if (warp == kCompWarp) {
+        if (lane == 0) {
+            const int nchunks = (nk + p.chunk - 1) / p.chunk;
+            for (int j = 0; j < nchunks; ++j) {
+                const int s = j % p.nc;
+                if (j >= p.nc && !mbar_wait(&hd->comp_empty[s], ring_prev_parity(j, p.nc), p.err, abort_flag))
+                    break;
+                const int i0 = j * p.chunk, i1 = min(nk, i0 + p.chunk), cn = i1 - i0;
+                uint8_t* slot = smem + p.off_c + (size_t)s * p.c_slot;
+                uint32_t hb[2] = {0, 0}, fb[2] = {0, 0}, bytes = 0;
+                int h0[2] = {0, 0}, f0[2] = {0, 0};
+                for (int sub = 0; sub < (has_g1 ? 2 : 1); ++sub) {
+                    const int2 a0 = offs[sub * ostride + i0], a1 = offs[sub * ostride + i1];
+                    h0[sub] = a0.x;
+                    f0[sub] = a0.y;
+                    hb[sub] = a1.x > a0.x ? (uint32_t)(a1.x - a0.x) : 0u;
+                    fb[sub] = a1.y > a0.y ? (uint32_t)(a1.y - a0.y) * 2u : 0u;
+                    if (hb[sub] > p.hf_cap || fb[sub] > p.full_cap || (hb[sub] & 15u) || (fb[sub] & 15u) ||
+                        (a0.x & 15) || (a0.y & 7) || a0.x < 0 || a0.y < 0) {
+                        if (p.err) atomicOr(p.err, kErrStreamOverflow);
+                        hb[sub] = min(hb[sub], p.hf_cap) & ~15u;
+                        fb[sub] = min(fb[sub], p.full_cap) & ~15u;
+                        h0[sub] = max(h0[sub], 0) & ~15;
+                        f0[sub] = max(f0[sub], 0) & ~7;
+                    }
+                    bytes += (3 * 512 + 32) * (uint32_t)cn + hb[sub] + fb[sub];
+                }
+                uint64_t* bar = &hd->comp_full[s];
+                ZS_STAMP(1 + j);
+                mbar_arrive_expect_tx(bar, bytes);
+                for (int sub = 0; sub < (has_g1 ? 2 : 1); ++sub) {
+                    const long long g = (long long)(gm0 + sub) * gtk + kb0 + i0;
+                    uint8_t* row = slot + sub * p.c_row;
+                    const uint32_t bmb = 512u * (uint32_t)cn;
+                    bulk_g2s(row, p.b1 + g * 64, bmb, bar);
+                    bulk_g2s(row + 512u * p.chunk, p.b2 + g * 64, bmb, bar);
+                    bulk_g2s(row + 1024u * p.chunk, p.b3 + g * 64, bmb, bar);
+                    bulk_g2s(row + p.c_mt, p.mt_off + g * 8, 32u * (uint32_t)cn, bar);
+                    if (hb[sub]) bulk_g2s(row + p.c_hf, p.sm + h0[sub], hb[sub], bar);
+                    if (fb[sub]) bulk_g2s(row + p.c_full, p.full + f0[sub], fb[sub], bar);
+                }
+            }
+        }
+    } else if (warp == kBWarp) {
         if (lane == 0) {
             for (int i = 0; i < nk; ++i) {
-                const int s = i % NS;
-                if (i >= NS && !mbar_wait(&hd->empty[s], ((i / NS) + 1) & 1, p.err, abort_flag)) break;
-                uint8_t* st = stages + (size_t)s * p.stage_bytes;
-                const int kb = kb0 + i;
-                const long long g0 = (long long)gm0 * gtk + kb;
-                GtCopy c0 = gt_copy_range(p.gt_off, g0, p.max_hf, p.max_full, p.err);
-                GtCopy c1{0, 0, 0u, 0u};
-                if (has_g1) c1 = gt_copy_range(p.gt_off, g0 + gtk, p.max_hf, p.max_full, p.err);
-                const uint32_t fixed = 3 * 512 + 32;
-                uint32_t bytes = (uint32_t)p.BN * 128u + fixed + c0.hb + c0.fb;
-                if (has_g1) bytes += fixed + c1.hb + c1.fb;
-                uint64_t* bar = &hd->full[s];
-                mbar_arrive_expect_tx(bar, bytes);
-                tma_load_2d(st + p.off_b, &tmap_x, kb * kGT, ntile * p.BN, bar);
-                for (int sub = 0; sub < (has_g1 ? 2 : 1); ++sub) {
-                    const long long g = g0 + sub * gtk;
-                    const GtCopy& c = sub ? c1 : c0;
-                    uint8_t* bm = st + p.off_bm + sub * 1536;
-                    bulk_g2s(bm, p.b1 + g * 64, 512, bar);
-                    bulk_g2s(bm + 512, p.b2 + g * 64, 512, bar);
-                    bulk_g2s(bm + 1024, p.b3 + g * 64, 512, bar);
-                    bulk_g2s(st + p.off_mt + sub * 32, p.mt_off + g * 8, 32, bar);
-                    if (c.hb) bulk_g2s(st + p.off_hf + sub * p.hf_slot, p.sm + c.h0, c.hb, bar);
-                    if (c.fb) bulk_g2s(st + p.off_full + sub * p.full_slot, p.full + c.f0, c.fb, bar);
-                }
+                const int s = i % p.nb;
+                if (i >= p.nb && !mbar_wait(&hd->b_empty[s], ring_prev_parity(i, p.nb), p.err, abort_flag)) break;
+                uint64_t* bar = &hd->b_full[s];
+                ZS_STAMP(20 + i);
+                mbar_arrive_expect_tx(bar, (uint32_t)p.BN * 128u);
+                tma_load_2d(smem + p.off_b + (size_t)s * p.b_slot, &tmap_x, (kb0 + i) * kGT, ntile * p.BN, bar);
             }
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_bf16(128, p.BN);
-            bool ok = true;
-            for (int i = 0; i < nk && ok; ++i) {
-                const int s = i % NS;
-                const uint32_t par = (i / NS) & 1;
-                ok = mbar_wait(&hd->full[s], par, p.err, abort_flag) &&
-                     mbar_wait(&hd->decoded[s], par, p.err, abort_flag);
-                if (!ok) break;
+            for (int i = 0; i < nk; ++i) {
+                const int sa = i % p.na, sb = i % p.nb;
+                if (!mbar_wait(&hd->a_full[sa], ring_parity(i, p.na), p.err, abort_flag) ||
+                    !mbar_wait(&hd->b_full[sb], ring_parity(i, p.nb), p.err, abort_flag))
+                    break;
+                ZS_STAMP(100 + i);
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(stages + (size_t)s * p.stage_bytes);
-                const uint32_t b_addr = a_addr + p.off_b;
+                const uint32_t a_tm = tmem_d + p.a_col + (uint32_t)sa * kASlotCols;
+                const uint32_t b_addr = smem_u32(smem + p.off_b + (size_t)sb * p.b_slot);
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    umma_bf16_ss(tmem_d, umma_desc_sw128(a_addr + 32 * k), umma_desc_sw128(b_addr + 32 * k), idesc,
+                    umma_bf16_ts(tmem_d, a_tm + 8u * k, umma_desc_sw128(b_addr + 32 * k), idesc,
                                  (i > 0 || k > 0) ? 1u : 0u);
-                umma_commit(&hd->empty[s]);
+                umma_commit(&hd->a_empty[sa]);
+                umma_commit(&hd->b_empty[sb]);
             }
             umma_commit(&hd->accum);
         }
     } else {
-        // decoders: warp = 4*group + q; q selects rows 32q..32q+31 of the tile
+        // decoders: warp = 4*group + q; q = TMEM lane quarter = rows 32q..32q+31
         const int group = warp >> 2, q = warp & 3, sub = q >> 1, half = q & 1;
         const DecodeTables tabs = make_decode_tables(p.start_exp);
         const bool active = (sub == 0) || has_g1;
-        for (int i = group; i < nk; i += 2) {
-            const int s = i % NS;
-            if (!mbar_wait(&hd->full[s], (i / NS) & 1, p.err, abort_flag)) break;
-            uint8_t* st = stages + (size_t)s * p.stage_bytes;
+        const uint32_t lut_lane = launder(smem_u32(lut)) + 4u * (uint32_t)lane;
+        const uint32_t smem0 = smem_u32(smem);
+        const uint32_t tlane = tmem_d + ((uint32_t)(32 * q) << 16) + p.a_col;
+        for (int i = group; i < nk; i += kDecodeGroups) {
+            const int jc = i / p.chunk, u = i - jc * p.chunk;
+            const int sc = jc % p.nc, sa = i % p.na;
+            if (!mbar_wait(&hd->comp_full[sc], ring_parity(jc, p.nc), p.err, abort_flag)) break;
+            if (i >= p.na && !mbar_wait(&hd->a_empty[sa], ring_prev_parity(i, p.na), p.err, abort_flag)) break;
+            tc_fence_after();
             if (active) {
-                GtSmem g;
-                g.bm1 = reinterpret_cast<const uint64_t*>(st + p.off_bm + sub * 1536);
-                g.bm2 = g.bm1 + 64;
-                g.bm3 = g.bm1 + 128;
-                g.mt = reinterpret_cast<const int*>(st + p.off_mt + sub * 32);
-                g.sm = st + p.off_hf + sub * p.hf_slot;
-                g.full = reinterpret_cast<const uint16_t*>(st + p.off_full + sub * p.full_slot);
-                g.hf_cap = p.hf_slot - 16;
-                g.full_cap = p.full_slot / 2 - 8;
-                uint8_t* a_tile = st + sub * 64 * 128;
-                decode_gt_half(g, lut, tabs, half, [&](int m, int kc, const uint32_t(&o)[4]) {
-                    *reinterpret_cast<uint4*>(a_tile + m * 128 + ((kc ^ (m & 7)) << 4)) =
-                        make_uint4(o[0], o[1], o[2], o[3]);
-                });
+                const uint32_t row = launder(smem0 + p.off_c + (uint32_t)sc * p.c_slot + (uint32_t)sub * p.c_row);
+                const int2 base = offs[sub * ostride + jc * p.chunk], cur = offs[sub * ostride + i];
+                const uint32_t hl = min((uint32_t)max(cur.x - base.x, 0), p.hf_cap);
+                const uint32_t fl = min((uint32_t)max(cur.y - base.y, 0) * 2u, p.full_cap);
+                GtView g;
+                g.bm = row + 512u * (uint32_t)u;
+                g.bstride = 512u * (uint32_t)p.chunk;
+                g.mt = row + p.c_mt + 32u * (uint32_t)u;
+                g.sm = row + p.c_hf + hl;
+                g.full = row + p.c_full + fl;
+                g.hf_cap = p.hf_cap - hl;
+                g.full_cap = (p.full_cap - fl) / 2;
+                const uint32_t ta = tlane + (uint32_t)sa * kASlotCols;
+                decode_gt_half_regs(g, lut_lane, tabs, half,
+                                    [&](int kc, uint32_t o0, uint32_t o1, uint32_t o2, uint32_t o3) {
+                                        tmem_st4(ta + 4u * (uint32_t)kc, o0, o1, o2, o3);
+                                    });
+                tmem_wait_st();
             }
-            fence_proxy_async_smem();
+            tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&hd->decoded[s]);
+            if (q == 0 && lane == 0) ZS_STAMP(60 + i);
+            if (lane == 0) {
+                mbar_arrive(&hd->a_full[sa]);
+                mbar_arrive(&hd->comp_empty[sc]);
+            }
         }
     }
 
+    // Single-thread roles (producers, MMA) must reconverge before the warp-wide
+    // .aligned cluster barriers below; otherwise the idle lanes sit in the
+    // barrier while lane 0 still runs its loop.
+    __syncwarp();
+
     // ---------------- epilogue: TMEM -> smem partial tile -> cluster reduce --
-    float* red = reinterpret_cast<float*>(stages);  // [BN][128] fp32, reuses the drained stages
+    // The partial tile reuses the ring area: all rings are drained once the
+    // accumulator is complete. Warps 0..3 cover the four TMEM lane quarters.
+    float* red = reinterpret_cast<float*>(smem + p.off_b);   // [BN][128] fp32
+    if (tid == 0) ZS_STAMP(220);
     if (warp < 4) {
         const int q = warp;
-        bool ok = (nk > 0) && mbar_wait(&hd->accum, 0, p.err, abort_flag);
+        const bool ok = (nk > 0) && mbar_wait(&hd->accum, 0, p.err, abort_flag);
         if (ok) {
             tc_fence_after();
             for (int c = 0; c < p.BN; c += 16) {
@@ -214,7 +306,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     }
     tc_fence_before();
+    if (tid == 0) ZS_STAMP(221);
     cluster_sync();
+    if (tid == 0) ZS_STAMP(222);
     {
         const int cols_per = (p.BN + S - 1) / S;
         const int nb = (int)rank * cols_per;
@@ -240,11 +334,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     }
     cluster_sync();
+    if (tid == 0) ZS_STAMP(223);
     if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem_d, p.tmem_cols);
     }
 }
+
+#ifdef ZS_TRACE
+extern "C" int zs_trace_set(unsigned long long* d_buf) {
+    return (int)cudaMemcpyToSymbol(g_zs_trace, &d_buf, sizeof(d_buf));
+}
+#endif
 
 // ------------------------------- host side ---------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
@@ -269,21 +370,29 @@ static uint32_t pow2_cols(int n) {
 struct DevInfo {
     int sms = 148;
     int max_smem = 232448;
+    bool attr_set = false;
 };
 
-static DevInfo dev_info() {
+// Per-device properties, and (once per device) the kernel attributes, so
+// launches made during CUDA-graph capture issue no attribute calls.
+static cudaError_t dev_setup(DevInfo* out) {
     static DevInfo info[64];
-    static bool have[64] = {};
     static std::mutex mu;
     int dev = 0;
-    cudaGetDevice(&dev);
+    ZS_RETURN_IF_ERR(cudaGetDevice(&dev));
+    if (dev >= 64) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> g(mu);
-    if (dev < 64 && !have[dev]) {
-        cudaDeviceGetAttribute(&info[dev].sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaDeviceGetAttribute(&info[dev].max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        have[dev] = true;
+    DevInfo& d = info[dev];
+    if (!d.attr_set) {
+        ZS_RETURN_IF_ERR(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+        ZS_RETURN_IF_ERR(cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        ZS_RETURN_IF_ERR(
+            cudaFuncSetAttribute(zipgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem));
+        ZS_RETURN_IF_ERR(cudaFuncSetAttribute(zipgemm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        d.attr_set = true;
     }
-    return dev < 64 ? info[dev] : DevInfo{};
+    *out = d;
+    return cudaSuccess;
 }
 
 cudaError_t launch_zipgemm(cudaStream_t stream, const uint8_t* sm, const uint16_t* full, const uint64_t* b1,
@@ -296,33 +405,22 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const uint8_t* sm, const uint16_
     if (!b1 || !b2 || !b3 || !mt_off || !gt_off || !X || !C) return cudaErrorInvalidValue;
     if ((max_hf > 0 && !sm) || (max_full > 0 && !full)) return cudaErrorInvalidValue;
     if (!aligned16(sm) || !aligned16(full) || !aligned16(b1) || !aligned16(b2) || !aligned16(b3) ||
-        !aligned16(mt_off) || !aligned16(X) || (reinterpret_cast<uintptr_t>(C) & 7u))
+        !aligned16(mt_off) || !aligned16(X) || (reinterpret_cast<uintptr_t>(C) & 7u) ||
+        (reinterpret_cast<uintptr_t>(gt_off) & 7u))
         return cudaErrorInvalidValue;
     auto encode = get_encode_fn();
     if (!encode) return cudaErrorNotSupported;
-    const DevInfo di = dev_info();
+    DevInfo di;
+    ZS_RETURN_IF_ERR(dev_setup(&di));
 
     GemmParams p{};
     p.sm = sm; p.full = full; p.b1 = b1; p.b2 = b2; p.b3 = b3; p.mt_off = mt_off; p.gt_off = gt_off;
     p.max_hf = max_hf; p.max_full = max_full; p.start_exp = start_exp & 0xFF;
     p.C = C; p.M = M; p.N = N; p.K = K; p.err = err;
     p.BN = std::min(256, (N + 15) / 16 * 16);
-    p.tmem_cols = pow2_cols(p.BN);
-    p.hf_slot = hf_slot_bytes(max_hf);
-    p.full_slot = full_slot_bytes(max_full);
-    p.off_b = 128 * 128;
-    p.off_bm = p.off_b + (uint32_t)p.BN * 128u;
-    p.off_mt = p.off_bm + 2 * 1536;
-    p.off_hf = p.off_mt + 64;
-    p.off_full = p.off_hf + 2 * p.hf_slot;
-    p.stage_bytes = round_up_u32(p.off_full + 2 * p.full_slot, 1024);
-    const uint32_t red_bytes = (uint32_t)p.BN * 128u * 4u;
-    int ns = (int)((di.max_smem - (int)kHeaderBytes) / (int)p.stage_bytes);
-    ns = std::min(ns, kMaxStages);
-    if (ns < 2) return cudaErrorInvalidValue;
-    p.nstages = ns;
-    if ((uint32_t)ns * p.stage_bytes < red_bytes) return cudaErrorInvalidValue;
-    const uint32_t smem_bytes = kHeaderBytes + (uint32_t)ns * p.stage_bytes;
+    p.tmem_cols = kTmemCols;
+    p.a_col = round_up_u32((uint32_t)p.BN, kASlotCols);
+    p.b_slot = (uint32_t)p.BN * 128u;
 
     const int mtiles = (M + 127) / 128;
     const int ntiles = (N + p.BN - 1) / p.BN;
@@ -332,6 +430,38 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const uint8_t* sm, const uint16_
     S = std::min(S, std::min(8, nkb));
     p.kb_per_split = (nkb + S - 1) / S;
     S = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // drop empty ranks
+
+    // Shared memory: header | spread table | staged offsets | B ring | A ring | compressed ring
+    const uint32_t offs_bytes = round_up_u32(2u * (uint32_t)(p.kb_per_split + 1) * 8u, 1024);
+    const uint32_t base = round_up_u32(kOffsOffset + offs_bytes, 1024);
+    const uint32_t budget = (uint32_t)di.max_smem - base;
+    p.na = (int)std::min<uint32_t>(kMaxRing, (kTmemCols - p.a_col) / kASlotCols);
+    p.nb = p.BN <= 128 ? 6 : 3;
+    const uint32_t hfc = round_up_u32((uint32_t)max_hf, 16), ffc = round_up_u32((uint32_t)max_full * 2u, 16);
+    auto slot_bytes = [&](int ch) {
+        const uint32_t row = round_up_u32((1536u + 32u) * ch + (hfc * ch + 16) + (ffc * ch + 16), 128);
+        return 2u * row;
+    };
+    uint32_t ab = (uint32_t)p.nb * p.b_slot;
+    while (p.nb > 2 && ab + 3 * slot_bytes(2) > budget) ab = (uint32_t)(--p.nb) * p.b_slot;
+    if (ab + 2 * slot_bytes(1) > budget) return cudaErrorInvalidValue;
+    // Largest chunk (<= 8 K blocks) that still leaves a double-buffered ring.
+    p.chunk = 1;
+    for (int ch = 8; ch > 1; --ch)
+        if (ab + 3 * slot_bytes(ch) <= budget) { p.chunk = ch; break; }
+    p.chunk = std::min(p.chunk, p.kb_per_split);
+    p.c_slot = slot_bytes(p.chunk);
+    p.c_row = p.c_slot / 2;
+    p.c_mt = 1536u * p.chunk;
+    p.c_hf = p.c_mt + 32u * p.chunk;
+    p.hf_cap = hfc * p.chunk;
+    p.c_full = p.c_hf + p.hf_cap + 16;
+    p.full_cap = ffc * p.chunk;
+    p.nc = (int)std::min<uint32_t>(kMaxRing, (budget - ab) / p.c_slot);
+    p.off_b = base;
+    p.off_c = p.off_b + (uint32_t)p.nb * p.b_slot;
+    const uint32_t smem_bytes = p.off_c + (uint32_t)p.nc * p.c_slot;
+    if (smem_bytes - p.off_b < (uint32_t)p.BN * 128u * 4u) return cudaErrorInvalidValue;
 
     CUtensorMap tmap;
     cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)N};
@@ -343,9 +473,6 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const uint8_t* sm, const uint16_
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return cudaErrorInvalidValue;
 
-    ZS_RETURN_IF_ERR(cudaFuncSetAttribute(zipgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem_bytes));
-    ZS_RETURN_IF_ERR(cudaFuncSetAttribute(zipgemm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)mtiles, (unsigned)S, (unsigned)ntiles);
     cfg.blockDim = dim3(kGemmThreads, 1, 1);
