@@ -81,6 +81,7 @@ struct GemmHeader {
     uint64_t a_full[kMaxRing], a_empty[kMaxRing];
     uint64_t b_full[kMaxRing], b_empty[kMaxRing];
     uint64_t accum;
+    uint64_t red_bar;   // peers' partial slices landed in this CTA's receive slots
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -145,6 +146,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int s = 0; s < p.na; ++s) { mbar_init(&hd->a_full[s], 4); mbar_init(&hd->a_empty[s], 1); }
         for (int s = 0; s < p.nb; ++s) { mbar_init(&hd->b_full[s], 1); mbar_init(&hd->b_empty[s], 1); }
         mbar_init(&hd->accum, 1);
+        mbar_init(&hd->red_bar, 1);
         hd->abort_flag = 0;
         fence_mbar_init();
     }
@@ -284,56 +286,84 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // barrier while lane 0 still runs its loop.
     __syncwarp();
 
-    // ---------------- epilogue: TMEM -> smem partial tile -> cluster reduce --
-    // The partial tile reuses the ring area: all rings are drained once the
-    // accumulator is complete. Warps 0..3 cover the four TMEM lane quarters.
-    float* red = reinterpret_cast<float*>(smem + p.off_b);   // [BN][128] fp32
-    if (tid == 0) ZS_STAMP(220);
-    if (warp < 4) {
-        const int q = warp;
-        const bool ok = (nk > 0) && mbar_wait(&hd->accum, 0, p.err, abort_flag);
-        if (ok) {
-            tc_fence_after();
-            for (int c = 0; c < p.BN; c += 16) {
-                uint32_t r[16];
-                tmem_ld16(tmem_d + ((uint32_t)(32 * q) << 16) + (uint32_t)c, r);
-                tmem_wait_ld();
+    // ---------------- epilogue: split-K reduction over the cluster -----------
+    // Columns of the BN-wide tile are split over the S cluster ranks. Each CTA
+    // drains its fp32 accumulator into its own shared memory ([BN][128], the
+    // drained ring area), then after one cluster barrier sends every other
+    // rank the slice that rank owns with one bulk copy (TMA engine, shared ->
+    // peer shared) into the receive slot reserved for this source rank. Each
+    // rank waits on its own mbarrier for the S-1 slices, sums the S partials of
+    // its columns in a fixed order (deterministic) and writes bf16.
+    // BN > 128 runs in passes of 128 columns so the buffers fit.
+    const int EB = min(p.BN, 128);
+    const int cols_per = (EB + S - 1) / S;
+    const int own_nb = (int)rank * cols_per;
+    const int own_cols = max(0, min(EB, own_nb + cols_per) - own_nb);
+    float* part = reinterpret_cast<float*>(smem + p.off_b);             // [EB][128] local partial
+    float* recv = part + (size_t)EB * 128;                               // [S][cols_per][128]
+    bool acc_ok = false;
+    if (warp < 4) acc_ok = (nk > 0) && mbar_wait(&hd->accum, 0, p.err, abort_flag);
+    for (int pass = 0; pass * EB < p.BN; ++pass) {
+        if (pass > 0) cluster_sync();   // every rank is done with the previous pass's buffers
+        if (warp < 4) {
+            const int q = warp;
+            if (acc_ok) {
+                tc_fence_after();
+                for (int c = 0; c < EB; c += 16) {
+                    uint32_t r[16];
+                    tmem_ld16(tmem_d + ((uint32_t)(32 * q) << 16) + (uint32_t)(pass * EB + c), r);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) red[(c + j) * 128 + 32 * q + lane] = __uint_as_float(r[j]);
+                    for (int j = 0; j < 16; ++j) part[(c + j) * 128 + 32 * q + lane] = __uint_as_float(r[j]);
+                }
+            } else {
+                for (int c = 0; c < EB; ++c) part[c * 128 + 32 * q + lane] = 0.f;
             }
-        } else {
-            for (int c = 0; c < p.BN; ++c) red[c * 128 + 32 * q + lane] = 0.f;
+            fence_proxy_async_smem();   // the bulk copies below read these values through the async proxy
         }
-    }
-    tc_fence_before();
-    if (tid == 0) ZS_STAMP(221);
-    cluster_sync();
-    if (tid == 0) ZS_STAMP(222);
-    {
-        const int cols_per = (p.BN + S - 1) / S;
-        const int nb = (int)rank * cols_per;
-        const int ncols = max(0, min(p.BN, nb + cols_per) - nb);
-        const uint32_t red_addr = smem_u32(red);
-        for (int idx = tid; idx < ncols * 32; idx += kGemmThreads) {
-            const int nl = nb + (idx >> 5), m4 = (idx & 31) * 4;
-            const int n = ntile * p.BN + nl;
-            const int m = mtile * 128 + m4;
-            if (n >= p.N || m >= p.M) continue;
-            const uint32_t off = (uint32_t)(nl * 128 + m4) * 4u;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int rr = 0; rr < S; ++rr) {
-                const float4 v = ld_dsmem_f4(mapa_shared(red_addr + off, (uint32_t)rr));
-                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        if (tid == 0 && S > 1) mbar_arrive_expect_tx(&hd->red_bar, (uint32_t)(S - 1) * (uint32_t)own_cols * 512u);
+        tc_fence_before();
+        if (tid == 0 && pass == 0) ZS_STAMP(220);
+        cluster_sync();
+        if (tid == 0 && pass == 0) ZS_STAMP(221);
+        if (tid == 0) {
+            for (int r2 = 0; r2 < S; ++r2) {
+                if (r2 == (int)rank) continue;
+                const int nb2 = r2 * cols_per, nc2 = max(0, min(EB, nb2 + cols_per) - nb2);
+                if (nc2 == 0) continue;
+                const uint32_t dst = smem_u32(recv + ((size_t)rank * cols_per) * 128);
+                bulk_s2peer(mapa_shared(dst, (uint32_t)r2), smem_u32(part + (size_t)nb2 * 128),
+                            (uint32_t)nc2 * 512u, mapa_shared(smem_u32(&hd->red_bar), (uint32_t)r2));
             }
-            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-            __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
-            uint2 pk;
-            pk.x = *reinterpret_cast<uint32_t*>(&lo);
-            pk.y = *reinterpret_cast<uint32_t*>(&hi);
-            *reinterpret_cast<uint2*>(p.C + (size_t)n * p.M + m) = pk;
+            bulk_commit();
         }
+        const bool got = (S == 1) || own_cols == 0 || mbar_wait(&hd->red_bar, (uint32_t)(pass & 1), p.err, abort_flag);
+        if (tid == 0 && pass == 0) ZS_STAMP(222);
+        if (got) {
+            for (int idx = tid; idx < own_cols * 32; idx += kGemmThreads) {
+                const int nl = idx >> 5, m4 = (idx & 31) * 4;
+                const int n = ntile * p.BN + pass * EB + own_nb + nl;
+                const int m = mtile * 128 + m4;
+                if (n >= p.N || m >= p.M) continue;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int sr = 0; sr < S; ++sr) {
+                    const float* src = (sr == (int)rank) ? part + (size_t)(own_nb + nl) * 128
+                                                         : recv + ((size_t)sr * cols_per + nl) * 128;
+                    const float4 v = *reinterpret_cast<const float4*>(src + m4);
+                    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                }
+                __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+                __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+                uint2 pk;
+                pk.x = *reinterpret_cast<uint32_t*>(&lo);
+                pk.y = *reinterpret_cast<uint32_t*>(&hi);
+                *reinterpret_cast<uint2*>(p.C + (size_t)n * p.M + m) = pk;
+            }
+        }
+        // our outgoing copies must finish reading `part` before it is reused or the CTA exits
+        if (tid == 0) bulk_wait_read0();
+        __syncthreads();
     }
-    cluster_sync();
     if (tid == 0) ZS_STAMP(223);
     if (warp == kMmaWarp) {
         tc_fence_after();
@@ -461,7 +491,9 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const uint8_t* sm, const uint16_
     p.off_b = base;
     p.off_c = p.off_b + (uint32_t)p.nb * p.b_slot;
     const uint32_t smem_bytes = p.off_c + (uint32_t)p.nc * p.c_slot;
-    if (smem_bytes - p.off_b < (uint32_t)p.BN * 128u * 4u) return cudaErrorInvalidValue;
+    const uint32_t eb = (uint32_t)std::min(p.BN, 128);
+    const uint32_t cols_per = (eb + (uint32_t)S - 1) / (uint32_t)S;
+    if (smem_bytes - p.off_b < (eb + (uint32_t)S * cols_per) * 512u) return cudaErrorInvalidValue;
 
     CUtensorMap tmap;
     cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)N};
