@@ -135,9 +135,9 @@ __device__ __forceinline__ void decode_gt_rows(const GtView& g, uint32_t lut_lan
 // tcgen05.st 32x32b wants: lane = row, 4 consecutive 32-bit columns per block.
 // The 8 blocks are processed in two phases of four so the shared-memory loads
 // of a phase are all issued before any of its values is consumed.
-template <class Emit>
+template <int NKC, class Emit>
 __device__ __forceinline__ void decode_gt_half_regs(const GtView& g, uint32_t lut_lane, const DecodeTables& t,
-                                                    int half, Emit&& emit) {
+                                                    int half, int kc0, Emit&& emit) {
     const int lane = threadIdx.x & 31;
     const int m = half * 32 + lane;
     const int w = m >> 4, mr = (m >> 3) & 1, r = m & 7;
@@ -146,14 +146,23 @@ __device__ __forceinline__ void decode_gt_half_regs(const GtView& g, uint32_t lu
     const uint32_t mhi = r < 4 ? 0u : ((1u << (8 * (r - 4))) - 1u);
     const uint32_t bsel = (uint32_t)(r & 3) | 0x4440u;
     const uint32_t bm = g.bm + 8u * (uint32_t)(w * 16 + mr);
-    uint32_t acc_h = lds32(g.mt + 8u * w);
-    uint32_t acc_f = lds32(g.mt + 8u * w + 4u);
+    // high-frequency elements in the column blocks before kc0 (both row blocks)
+    uint32_t skipped = 0;
+    for (int kc = 0; kc < kc0; ++kc) {
+        const uint32_t bo = bm + 16u * (uint32_t)kc;
+        const uint2 v1 = lds64(bo), v2 = lds64(bo + g.bstride), v3 = lds64(bo + 2u * g.bstride);
+        const uint32_t tot = __popc(v1.x | v2.x | v3.x) + __popc(v1.y | v2.y | v3.y);
+        skipped += tot + __shfl_xor_sync(0xFFFFFFFFu, tot, 8);
+    }
+    uint32_t acc_h = lds32(g.mt + 8u * w) + skipped;
+    uint32_t acc_f = lds32(g.mt + 8u * w + 4u) + 128u * (uint32_t)kc0 - skipped;
+    constexpr int PH = NKC < 4 ? NKC : 4;
 #pragma unroll
-    for (int ph = 0; ph < 2; ++ph) {
-        uint32_t c1[4], c2[4], c3[4], hf[4], fo[4];
+    for (int ph = 0; ph < NKC / PH; ++ph) {
+        uint32_t c1[PH], c2[PH], c3[PH], hf[PH], fo[PH];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint32_t bo = bm + 16u * (uint32_t)(4 * ph + u);
+        for (int u = 0; u < PH; ++u) {
+            const uint32_t bo = bm + 16u * (uint32_t)(kc0 + PH * ph + u);
             const uint2 v1 = lds64(bo), v2 = lds64(bo + g.bstride), v3 = lds64(bo + 2u * g.bstride);
             const uint32_t ilo = v1.x | v2.x | v3.x;
             const uint32_t ihi = v1.y | v2.y | v3.y;
@@ -169,9 +178,9 @@ __device__ __forceinline__ void decode_gt_half_regs(const GtView& g, uint32_t lu
             acc_h += tot + ptot;
             acc_f += 128u - tot - ptot;
         }
-        uint32_t s1[4], s2[4], s3[4], q0[4], q1[4], q2[4];
+        uint32_t s1[PH], s2[PH], s3[PH], q0[PH], q1[PH], q2[PH];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < PH; ++u) {
             s1[u] = lds32(lut_lane + (c1[u] << 7));
             s2[u] = lds32(lut_lane + (c2[u] << 7));
             s3[u] = lds32(lut_lane + (c3[u] << 7));
@@ -181,7 +190,7 @@ __device__ __forceinline__ void decode_gt_half_regs(const GtView& g, uint32_t lu
             q2[u] = lds32(wa + 8);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < PH; ++u) {
             const uint32_t X = s1[u] + (s2[u] << 1) + (s3[u] << 2);
             const uint32_t sel = (s1[u] | s2[u] | s3[u]) * 0x11111110u;
             const uint32_t sh = ((g.sm + hf[u]) & 3u) * 8u;
@@ -212,7 +221,7 @@ __device__ __forceinline__ void decode_gt_half_regs(const GtView& g, uint32_t lu
                     o3 = pj == 3 ? (o3 & keep) | ins : o3;
                 } while (fm);
             }
-            emit(4 * ph + u, o0, o1, o2, o3);
+            emit(kc0 + PH * ph + u, o0, o1, o2, o3);
         }
     }
 }

@@ -39,8 +39,10 @@
 
 namespace zs {
 
-constexpr int kDecodeGroups = 6;
-constexpr int kDecodeWarps = 4 * kDecodeGroups;
+constexpr int kKSplit = 1;                          // warps per GT-half row block (column split)
+constexpr int kDecodeGroups = 6 / kKSplit;          // groups of 4 * kKSplit warps, one K block each
+constexpr int kGroupWarps = 4 * kKSplit;
+constexpr int kDecodeWarps = kGroupWarps * kDecodeGroups;
 constexpr int kCompWarp = kDecodeWarps;
 constexpr int kBWarp = kDecodeWarps + 1;
 constexpr int kMmaWarp = kDecodeWarps + 2;
@@ -141,9 +143,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if ((smem_u32(smem) & 1023u) && p.err) atomicOr(p.err, kErrStreamOverflow);
         for (int s = 0; s < p.nc; ++s) {
             mbar_init(&hd->comp_full[s], 1);
-            mbar_init(&hd->comp_empty[s], 4 * p.chunk);   // every K block of the chunk, 4 warps each
+            mbar_init(&hd->comp_empty[s], kGroupWarps * p.chunk);   // every K block of the chunk, each group warp
         }
-        for (int s = 0; s < p.na; ++s) { mbar_init(&hd->a_full[s], 4); mbar_init(&hd->a_empty[s], 1); }
+        for (int s = 0; s < p.na; ++s) { mbar_init(&hd->a_full[s], kGroupWarps); mbar_init(&hd->a_empty[s], 1); }
         for (int s = 0; s < p.nb; ++s) { mbar_init(&hd->b_full[s], 1); mbar_init(&hd->b_empty[s], 1); }
         mbar_init(&hd->accum, 1);
         mbar_init(&hd->red_bar, 1);
@@ -238,8 +240,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             umma_commit(&hd->accum);
         }
     } else {
-        // decoders: warp = 4*group + q; q = TMEM lane quarter = rows 32q..32q+31
-        const int group = warp >> 2, q = warp & 3, sub = q >> 1, half = q & 1;
+        // decoders: warp = kGroupWarps*group + 4*ks + q; q = TMEM lane quarter =
+        // rows 32q..32q+31; ks selects column blocks [ks*8/kKSplit, (ks+1)*8/kKSplit)
+        const int group = warp / kGroupWarps, ks = (warp % kGroupWarps) >> 2, q = warp & 3;
+        const int sub = q >> 1, half = q & 1;
         const DecodeTables tabs = make_decode_tables(p.start_exp);
         const bool active = (sub == 0) || has_g1;
         const uint32_t lut_lane = launder(smem_u32(lut)) + 4u * (uint32_t)lane;
@@ -265,7 +269,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 g.hf_cap = p.hf_cap - hl;
                 g.full_cap = (p.full_cap - fl) / 2;
                 const uint32_t ta = tlane + (uint32_t)sa * kASlotCols;
-                decode_gt_half_regs(g, lut_lane, tabs, half,
+                decode_gt_half_regs<8 / kKSplit>(g, lut_lane, tabs, half, ks * (8 / kKSplit),
                                     [&](int kc, uint32_t o0, uint32_t o1, uint32_t o2, uint32_t o3) {
                                         tmem_st4(ta + 4u * (uint32_t)kc, o0, o1, o2, o3);
                                     });
@@ -273,7 +277,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (q == 0 && lane == 0) ZS_STAMP(60 + i);
+            if (warp % kGroupWarps == 0 && lane == 0) ZS_STAMP(60 + i);
             if (lane == 0) {
                 mbar_arrive(&hd->a_full[sa]);
                 mbar_arrive(&hd->comp_empty[sc]);
