@@ -69,6 +69,29 @@ int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const 
                int max_hf, int max_full, int start_exp, const uint16_t* d_x, uint16_t* d_c, int M, int N,
                int K, int split_k, unsigned* d_err);
 
+/* Workspace (device bytes) needed by zs_decode_attention for a split count
+ * (0 when num_splits <= 1). */
+size_t zs_decode_attention_workspace_bytes(int B, int Hq, int Hkv, int num_splits);
+
+/* Compressed-KV decode attention, one query token per sequence:
+ *   out[b][h] = softmax(q[b][h] . K[b][h/G]^T * softmax_scale) . V[b][h/G],  G = Hq / Hkv,
+ * over the first d_seqlens[b] tokens. K and V are TCA-TBE compressed matrices
+ * of B*Hkv*T_pad rows x D columns in head-major order (row (b*Hkv + h)*T_pad + t,
+ * T_pad % 64 == 0, D == 128). k_ptrs / v_ptrs: host arrays of the 7 device
+ * stream pointers {sign_mantissa, compressed_full, bitmap1, bitmap2, bitmap3,
+ * tile_offsets_median, tile_offsets_global}; k_meta / v_meta: host arrays
+ * {rows, cols, max_high_freq_count, max_full_count, start_exp}. q and out are
+ * [B][Hq][D] bf16. max_seqlen bounds d_seqlens (host value). num_splits <= 0
+ * picks the split-KV factor automatically; for more than one split d_ws must
+ * hold zs_decode_attention_workspace_bytes(...) bytes. *splits_used (nullable)
+ * receives the split count. Replaces the ZipServ decode path of FlashAttention
+ * (FA csrc/flash_attn/flash_api.cpp:1346 mha_fwd_kvcache with zipserv_k/_v,
+ * FA flash_attn/flash_attn_interface.py:1592 flash_attn_with_kvcache). */
+int zs_decode_attention(void* stream, const uint16_t* d_q, const void* const* k_ptrs, const int* k_meta,
+                        const void* const* v_ptrs, const int* v_meta, const int* d_seqlens, int B, int Hq, int Hkv,
+                        int D, int T_pad, int max_seqlen, float softmax_scale, int num_splits, float* d_ws,
+                        size_t ws_bytes, uint16_t* d_out, int* splits_used, unsigned* d_err);
+
 #ifdef __cplusplus
 }
 #endif

@@ -6,3 +6,6 @@ modules here are thin torch-facing wrappers over its C ABI."""
 from .codec import Compressed, analyze_exponents, compress, decompress, zipgemm  # noqa: F401
 
 __all__ = ["Compressed", "analyze_exponents", "compress", "decompress", "zipgemm"]
+from .attention import compress_kv, decode_attention, flash_attn_with_kvcache, pad_kv_by_kv_head  # noqa: E402,F401
+
+__all__ += ["compress_kv", "decode_attention", "flash_attn_with_kvcache", "pad_kv_by_kv_head"]

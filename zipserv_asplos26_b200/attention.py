@@ -1,0 +1,127 @@
+"""Compressed-KV decode attention (torch-facing).
+
+Mirrors the ZipServ decode path of the reference:
+  * pad_kv_by_kv_head  -> kernel_benchmark/bench_zipserv_decode_attention.py:347
+                          pad_batched_kv_prefix_by_kv_head ([B,T,Hkv,D] -> head-major 2-D)
+  * compress_kv        -> the ext's compress_zipserv on that padded matrix
+  * decode_attention   -> FA flash_attn_with_kvcache(q, ..., zipserv_k=, zipserv_v=,
+                          zipserv_num_heads_k=) (FA flash_attn_interface.py:1592-1754)
+  * flash_attn_with_kvcache -> the same call signature subset, taking the
+                          reference's descriptor dicts (FA flash_attn_interface.py:23-36)
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import Optional
+
+import torch
+
+from ._lib import check, lib
+from .codec import Compressed, compress
+
+_FIELDS = ("sign_mantissa", "compressed_full", "bitmap1", "bitmap2", "bitmap3", "tile_offsets_median",
+           "tile_offsets_global")
+
+
+def pad_kv_by_kv_head(x: torch.Tensor):
+    """[B, T, Hkv, D] -> ([B*Hkv*T_pad, D_pad] zero padded, rows, T_pad)."""
+    B, T, Hkv, D = x.shape
+    t_pad = (T + 63) // 64 * 64
+    d_pad = (D + 63) // 64 * 64
+    out = torch.zeros((B, Hkv, t_pad, d_pad), dtype=x.dtype, device=x.device)
+    out[:, :, :T, :D] = x.permute(0, 2, 1, 3)
+    return out.view(B * Hkv * t_pad, d_pad), B * Hkv * t_pad, t_pad
+
+
+def compress_kv(x: torch.Tensor, rule: str = "ext") -> Compressed:
+    """Compress a [B, T, Hkv, D] K or V cache in the head-major 64-token page layout."""
+    flat, _, _ = pad_kv_by_kv_head(x)
+    return compress(flat, rule=rule)
+
+
+def _ptrs_meta(c: Compressed):
+    ptrs = (C.c_void_p * 7)(*[getattr(c, f).data_ptr() for f in _FIELDS])
+    meta = (C.c_int * 5)(c.rows, c.cols, c.max_high_freq_count, c.max_full_count, c.start_exp)
+    return ptrs, meta
+
+
+def decode_attention(q: torch.Tensor, k: Compressed, v: Compressed, cache_seqlens: torch.Tensor,
+                     num_heads_k: int, softmax_scale: Optional[float] = None, num_splits: int = 0,
+                     max_seqlen: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q: [B, Hq, D] (or [B, 1, Hq, D]) bf16; returns the same shape."""
+    squeeze = q.dim() == 4
+    q3 = q.reshape(q.shape[0], q.shape[-2], q.shape[-1]) if squeeze else q
+    if q3.dtype != torch.bfloat16 or not q3.is_cuda:
+        raise ValueError("q must be a bf16 CUDA tensor")
+    q3 = q3.contiguous()
+    B, Hq, D = q3.shape
+    if Hq % num_heads_k:
+        raise ValueError("num_heads must be a multiple of num_heads_k")
+    if k.rows % (B * num_heads_k) or k.rows != v.rows or k.cols != v.cols:
+        raise ValueError("K/V row count must be B * num_heads_k * T_pad and agree")
+    t_pad = k.rows // (B * num_heads_k)
+    seq = cache_seqlens.to(device=q3.device, dtype=torch.int32).contiguous()
+    if max_seqlen is None:
+        max_seqlen = int(seq.max().item()) if seq.numel() else 0
+    max_seqlen = min(max_seqlen, t_pad)
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    L = lib()
+    splits = num_splits
+    if splits <= 0:
+        sms = torch.cuda.get_device_properties(q3.device).multi_processor_count
+        splits = max(1, min((2 * sms + B * num_heads_k - 1) // (B * num_heads_k), (max_seqlen + 63) // 64))
+    ws_bytes = L.zs_decode_attention_workspace_bytes(B, Hq, num_heads_k, splits)
+    ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device=q3.device)
+    if out is None:
+        out = torch.empty_like(q3)
+    kp, km = _ptrs_meta(k)
+    vp, vm = _ptrs_meta(v)
+    used = C.c_int(0)
+    check(L.zs_decode_attention(torch.cuda.current_stream().cuda_stream, q3.data_ptr(), kp, km, vp, vm,
+                                seq.data_ptr(), B, Hq, num_heads_k, D, t_pad, max_seqlen, scale, splits,
+                                ws.data_ptr(), ws_bytes, out.data_ptr(), C.byref(used), None),
+          "zs_decode_attention")
+    return out.view(q.shape) if squeeze else out
+
+
+def _as_compressed(desc, device) -> Compressed:
+    if isinstance(desc, Compressed):
+        return desc
+    if isinstance(desc, dict):
+        vals = {f: desc[f] for f in _FIELDS}
+        rows, cols = int(desc["rows"]), int(desc["cols"])
+        mh, mf, se = int(desc["max_high_freq_count"]), int(desc["max_full_count"]), int(desc["start_exp"])
+    else:  # sequence in the reference's field order (FA flash_attn_interface.py:23-36)
+        vals = dict(zip(_FIELDS, desc[:7]))
+        rows, cols, mh, mf, se = (int(x) for x in desc[7:12])
+    for f, t in vals.items():
+        if not isinstance(t, torch.Tensor) or t.device != device:
+            raise ValueError(f"{f} must be a tensor on {device}")
+    return Compressed(vals["sign_mantissa"], vals["compressed_full"], vals["bitmap1"], vals["bitmap2"],
+                      vals["bitmap3"], None, vals["tile_offsets_median"], vals["tile_offsets_global"], rows, cols,
+                      mh, mf, se & 0xFF, 0, 0)
+
+
+def flash_attn_with_kvcache(q, k_cache=None, v_cache=None, cache_seqlens=None, softmax_scale=None,
+                            num_splits=0, zipserv_k=None, zipserv_v=None, zipserv_num_heads_k=None, **unused):
+    """Decode-attention entry with the reference's ZipServ keyword arguments.
+
+    q is [B, 1, Hq, D]; zipserv_k / zipserv_v are descriptors as accepted by the
+    reference (dict with the 12 fields, or a sequence in that order, layout
+    "by_kv_head"). Only the compressed path is provided here."""
+    if zipserv_k is None or zipserv_v is None:
+        raise ValueError("zipserv_k and zipserv_v are required")
+    for d in (zipserv_k, zipserv_v):
+        if isinstance(d, dict) and d.get("layout", "by_kv_head") != "by_kv_head":
+            raise ValueError("only the by_kv_head layout is implemented")
+    hk = zipserv_num_heads_k if zipserv_num_heads_k else (k_cache.shape[2] if k_cache is not None else 0)
+    if not hk:
+        raise ValueError("zipserv_num_heads_k must be provided")
+    k = _as_compressed(zipserv_k, q.device)
+    v = _as_compressed(zipserv_v, q.device)
+    if cache_seqlens is None:
+        cache_seqlens = torch.full((q.shape[0],), k.rows // (q.shape[0] * hk), dtype=torch.int32, device=q.device)
+    elif not isinstance(cache_seqlens, torch.Tensor):
+        cache_seqlens = torch.full((q.shape[0],), int(cache_seqlens), dtype=torch.int32, device=q.device)
+    return decode_attention(q, k, v, cache_seqlens, hk, softmax_scale, num_splits)

@@ -82,6 +82,38 @@ extern "C" int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_f
                               max_full, start_exp, d_x, d_c, M, N, K, split_k, d_err);
 }
 
+extern "C" size_t zs_decode_attention_workspace_bytes(int B, int Hq, int Hkv, int num_splits) {
+    return zs::attn_workspace_bytes(B, Hq, Hkv, num_splits);
+}
+
+static bool to_compressed(const void* const* ptrs, const int* meta, zs::AttnCompressed* c) {
+    if (!ptrs || !meta) return false;
+    c->sm = static_cast<const uint8_t*>(ptrs[0]);
+    c->full = static_cast<const uint16_t*>(ptrs[1]);
+    c->b1 = static_cast<const uint64_t*>(ptrs[2]);
+    c->b2 = static_cast<const uint64_t*>(ptrs[3]);
+    c->b3 = static_cast<const uint64_t*>(ptrs[4]);
+    c->mt_off = static_cast<const int*>(ptrs[5]);
+    c->gt_off = static_cast<const int*>(ptrs[6]);
+    c->rows = meta[0];
+    c->cols = meta[1];
+    c->max_hf = meta[2];
+    c->max_full = meta[3];
+    c->start_exp = meta[4];
+    return true;
+}
+
+extern "C" int zs_decode_attention(void* stream, const uint16_t* d_q, const void* const* k_ptrs, const int* k_meta,
+                                   const void* const* v_ptrs, const int* v_meta, const int* d_seqlens, int B, int Hq,
+                                   int Hkv, int D, int T_pad, int max_seqlen, float softmax_scale, int num_splits,
+                                   float* d_ws, size_t ws_bytes, uint16_t* d_out, int* splits_used,
+                                   unsigned* d_err) {
+    zs::AttnCompressed k{}, v{};
+    if (!to_compressed(k_ptrs, k_meta, &k) || !to_compressed(v_ptrs, v_meta, &v)) return cudaErrorInvalidValue;
+    return zs::launch_attention((cudaStream_t)stream, k, v, d_q, d_seqlens, d_out, B, Hq, Hkv, D, T_pad, max_seqlen,
+                                softmax_scale, num_splits, d_ws, ws_bytes, d_err, splits_used);
+}
+
 // ---------------------- reference GPU ABI (C++ names) -----------------------
 cudaError_t BF16TripleBitmap_MM_API(cudaStream_t stream, const uint8_t* SignMantissa,
                                     const __nv_bfloat16* CompressedFull, const uint64_t* Bitmap1,

@@ -34,4 +34,23 @@ cudaError_t launch_zipgemm(cudaStream_t s, const uint8_t* sm, const uint16_t* fu
                            int max_hf, int max_full, int start_exp, const uint16_t* X, uint16_t* C, int M,
                            int N, int K, int split_k, unsigned* err);
 
+// One TCA-TBE compressed matrix (device pointers + scalars).
+struct AttnCompressed {
+    const uint8_t* sm;
+    const uint16_t* full;
+    const uint64_t* b1;
+    const uint64_t* b2;
+    const uint64_t* b3;
+    const int* mt_off;
+    const int* gt_off;
+    int rows, cols, max_hf, max_full, start_exp;
+};
+
+size_t attn_workspace_bytes(int B, int Hq, int Hkv, int num_splits);
+
+cudaError_t launch_attention(cudaStream_t s, const AttnCompressed& k, const AttnCompressed& v, const uint16_t* q,
+                             const int* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int T_pad,
+                             int max_seqlen, float softmax_scale, int num_splits, float* ws, size_t ws_bytes,
+                             unsigned* err, int* splits_used);
+
 }  // namespace zs
