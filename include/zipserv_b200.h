@@ -92,6 +92,24 @@ int zs_decode_attention(void* stream, const uint16_t* d_q, const void* const* k_
                         int D, int T_pad, int max_seqlen, float softmax_scale, int num_splits, float* d_ws,
                         size_t ws_bytes, uint16_t* d_out, int* splits_used, unsigned* d_err);
 
+/* Allocation-free decode attention (no counterpart in the reference).
+ * For callers that cannot allocate device memory when they run attention
+ * (code running inside an allocator's own hooks, or deployments that forbid
+ * cudaMalloc after start-up to keep a fixed memory budget): same inputs,
+ * outputs and results as zs_decode_attention, but the split-KV workspace is a
+ * fixed device array inside the library (2 MiB per GPU, held until exit), so
+ * the caller passes no workspace and nothing is allocated. Returns
+ * cudaErrorInvalidValue when B * Hq * splits * (D + 2) * 4 bytes exceeds
+ * zs_decode_attention_noalloc_max_workspace_bytes(). The first call on a
+ * device looks up the array's address on that device; make that first call
+ * outside any stream capture. All calls share the array: calls that overlap on
+ * the GPU (unordered streams) race; order them on one stream. */
+size_t zs_decode_attention_noalloc_max_workspace_bytes(void);
+int zs_decode_attention_noalloc(void* stream, const uint16_t* d_q, const void* const* k_ptrs, const int* k_meta,
+                                const void* const* v_ptrs, const int* v_meta, const int* d_seqlens, int B, int Hq,
+                                int Hkv, int D, int T_pad, int max_seqlen, float softmax_scale, int num_splits,
+                                uint16_t* d_out, int* splits_used, unsigned* d_err);
+
 #ifdef __cplusplus
 }
 #endif

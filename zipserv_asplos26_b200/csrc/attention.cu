@@ -22,6 +22,7 @@
 // workspace and combine_kernel merges the splits; with S = 1 the CTA writes
 // the normalised bf16 output itself.
 #include <algorithm>
+#include <mutex>
 #include <cmath>
 #include <cstddef>
 
@@ -426,6 +427,61 @@ cudaError_t launch_attention(cudaStream_t stream, const AttnCompressed& kc, cons
         ZS_RETURN_IF_ERR(cudaGetLastError());
     }
     return cudaSuccess;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of launch_attention.
+//
+// Some callers cannot allocate device memory at the point where they run
+// attention: code that executes while an allocator is not available (for
+// example inside a custom memory pool's own callbacks, or in an embedding that
+// forbids cudaMalloc after start-up so its memory budget stays fixed). For them
+// the split-KV workspace lives in this file-scope device array instead of a
+// caller buffer. It is created when the library is loaded on a GPU and kept
+// until the process exits (kNoAllocWsFloats * 4 bytes = 2 MiB per GPU).
+//
+// Every call on a device shares the same array and leaves the last call's
+// partial results in it. Nothing in it has to start at zero: each split writes
+// all of its slots before the combine kernel reads them. Two calls whose
+// kernels overlap on the GPU (different streams, no ordering between them)
+// race on the array and may return wrong results; order them on one stream.
+constexpr size_t kNoAllocWsFloats = 512 * 1024;
+static __device__ __align__(256) float g_attn_noalloc_ws[kNoAllocWsFloats];
+
+// The array's device address for the current device, looked up once per
+// device (cudaGetSymbolAddress with that device current). The first call on a
+// device does this look-up; make that first call outside any stream capture.
+static cudaError_t noalloc_ws_ptr(float** out) {
+    static float* ptrs[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    ZS_RETURN_IF_ERR(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(mu);
+    if (!ptrs[dev]) {
+        void* ptr = nullptr;
+        ZS_RETURN_IF_ERR(cudaGetSymbolAddress(&ptr, g_attn_noalloc_ws));
+        ptrs[dev] = static_cast<float*>(ptr);
+    }
+    *out = ptrs[dev];
+    return cudaSuccess;
+}
+
+size_t attn_noalloc_ws_bytes() { return kNoAllocWsFloats * sizeof(float); }
+
+cudaError_t launch_attention_noalloc(cudaStream_t stream, const AttnCompressed& k, const AttnCompressed& v,
+                                     const uint16_t* q, const int* seqlens, uint16_t* out, int B, int Hq, int Hkv,
+                                     int D, int T_pad, int max_seqlen, float softmax_scale, int num_splits,
+                                     unsigned* err, int* splits_used) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || max_seqlen < 0) return cudaErrorInvalidValue;
+    const int max_pages = std::max(1, (max_seqlen + 63) / 64);
+    const int S = num_splits > 0 ? std::min(num_splits, max_pages) : attn_default_splits(B, Hkv, max_pages);
+    // Sizes whose split workspace does not fit the fixed array are rejected.
+    if (attn_workspace_bytes(B, Hq, Hkv, S) > attn_noalloc_ws_bytes()) return cudaErrorInvalidValue;
+    float* ws = nullptr;
+    ZS_RETURN_IF_ERR(noalloc_ws_ptr(&ws));
+    return launch_attention(stream, k, v, q, seqlens, out, B, Hq, Hkv, D, T_pad, max_seqlen, softmax_scale, S, ws,
+                            attn_noalloc_ws_bytes(), err, splits_used);
 }
 
 }  // namespace zs

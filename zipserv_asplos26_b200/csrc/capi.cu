@@ -114,6 +114,19 @@ extern "C" int zs_decode_attention(void* stream, const uint16_t* d_q, const void
                                 softmax_scale, num_splits, d_ws, ws_bytes, d_err, splits_used);
 }
 
+extern "C" size_t zs_decode_attention_noalloc_max_workspace_bytes(void) { return zs::attn_noalloc_ws_bytes(); }
+
+extern "C" int zs_decode_attention_noalloc(void* stream, const uint16_t* d_q, const void* const* k_ptrs,
+                                           const int* k_meta, const void* const* v_ptrs, const int* v_meta,
+                                           const int* d_seqlens, int B, int Hq, int Hkv, int D, int T_pad,
+                                           int max_seqlen, float softmax_scale, int num_splits, uint16_t* d_out,
+                                           int* splits_used, unsigned* d_err) {
+    zs::AttnCompressed k{}, v{};
+    if (!to_compressed(k_ptrs, k_meta, &k) || !to_compressed(v_ptrs, v_meta, &v)) return cudaErrorInvalidValue;
+    return zs::launch_attention_noalloc((cudaStream_t)stream, k, v, d_q, d_seqlens, d_out, B, Hq, Hkv, D, T_pad,
+                                        max_seqlen, softmax_scale, num_splits, d_err, splits_used);
+}
+
 // ---------------------- reference GPU ABI (C++ names) -----------------------
 cudaError_t BF16TripleBitmap_MM_API(cudaStream_t stream, const uint8_t* SignMantissa,
                                     const __nv_bfloat16* CompressedFull, const uint64_t* Bitmap1,

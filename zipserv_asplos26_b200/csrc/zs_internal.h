@@ -53,4 +53,10 @@ cudaError_t launch_attention(cudaStream_t s, const AttnCompressed& k, const Attn
                              int max_seqlen, float softmax_scale, int num_splits, float* ws, size_t ws_bytes,
                              unsigned* err, int* splits_used);
 
+size_t attn_noalloc_ws_bytes();
+cudaError_t launch_attention_noalloc(cudaStream_t s, const AttnCompressed& k, const AttnCompressed& v,
+                                     const uint16_t* q, const int* seqlens, uint16_t* out, int B, int Hq, int Hkv,
+                                     int D, int T_pad, int max_seqlen, float softmax_scale, int num_splits,
+                                     unsigned* err, int* splits_used);
+
 }  // namespace zs
