@@ -1,0 +1,118 @@
+"""Tensor-parallel ZipGEMM layers (new relative to the reference, which has no
+collectives): column-parallel projections (QKV, gate_up) split W by output rows
+and need no communication; row-parallel projections (O, down) split W by K and
+sum the per-rank partial outputs with one all-reduce (NCCL over NVLink on GPUs;
+any torch.distributed backend works, gloo is used by the CPU tests).
+
+Each rank compresses only its own shard (its own exponent window), exactly as a
+per-rank checkpoint would be compressed."""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+
+def _rank_world(group=None):
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group), dist.get_world_size(group)
+    return 0, 1
+
+
+def shard_rows(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Rows [M/world * rank, M/world * (rank+1)) of W (column-parallel shard)."""
+    M = w.shape[0]
+    if M % world or (M // world) % 64:
+        raise ValueError(f"M={M} must split into multiples of 64 over {world} ranks")
+    m = M // world
+    return w[rank * m:(rank + 1) * m].contiguous()
+
+
+def shard_cols(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Columns [K/world * rank, ...) of W (row-parallel shard)."""
+    K = w.shape[1]
+    if K % world or (K // world) % 64:
+        raise ValueError(f"K={K} must split into multiples of 64 over {world} ranks")
+    k = K // world
+    return w[:, rank * k:(rank + 1) * k].contiguous()
+
+
+def _zipgemm_backend(c, x, out=None):
+    from .codec import zipgemm
+    return zipgemm(c, x, out=out)
+
+
+def _compress_backend(w):
+    from .codec import compress
+    return compress(w)
+
+
+class ColumnParallelZipLinear:
+    """y_local[N, M/world] = x[N, K] @ W_shard^T; no collective."""
+
+    def __init__(self, w_shard: torch.Tensor, gemm: Callable = _zipgemm_backend,
+                 compressor: Callable = _compress_backend, group=None):
+        self.gemm = gemm
+        self.group = group
+        self.weight = compressor(w_shard)
+        self.out_features = w_shard.shape[0]
+        self.in_features = w_shard.shape[1]
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return self.gemm(self.weight, x, out=out)
+
+
+class RowParallelZipLinear:
+    """y[N, M] = sum over ranks of x_local[N, K/world] @ W_shard^T (all-reduce)."""
+
+    def __init__(self, w_shard: torch.Tensor, gemm: Callable = _zipgemm_backend,
+                 compressor: Callable = _compress_backend, group=None):
+        self.gemm = gemm
+        self.group = group
+        self.weight = compressor(w_shard)
+        self.out_features = w_shard.shape[0]
+        self.in_features = w_shard.shape[1]
+
+    def __call__(self, x_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        y = self.gemm(self.weight, x_local, out=out)
+        _, world = _rank_world(self.group)
+        if world > 1:
+            dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+        return y
+
+
+# Llama-3.1-70B projection shapes: (out_features, in_features)
+LLAMA70B_SHAPES = {"qkv": (10240, 8192), "o": (8192, 8192), "gate_up": (57344, 8192), "down": (8192, 28672)}
+LLAMA8B_SHAPES = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (28672, 4096), "down": (4096, 14336)}
+
+
+class TPLayerGemms:
+    """The four weight GEMMs of one decoder layer, tensor-parallel:
+    QKV and gate_up column-parallel, O and down row-parallel (+ all-reduce).
+    Weights are generated per rank from a seed (synthetic, N(0, sigma))."""
+
+    def __init__(self, shapes=LLAMA70B_SHAPES, seed: int = 0, sigma: float = 0.02, device=None,
+                 gemm: Callable = _zipgemm_backend, compressor: Callable = _compress_backend,
+                 dtype=torch.bfloat16, group=None):
+        rank, world = _rank_world(group)
+        self.rank, self.world = rank, world
+        self.layers = {}
+        for i, (name, (M, K)) in enumerate(shapes.items()):
+            col = name in ("qkv", "gate_up")
+            m = M // world if col else M
+            k = K if col else K // world
+            if (m % 64) or (k % 64):
+                raise ValueError(f"{name}: shard {m}x{k} is not a multiple of 64")
+            g = torch.Generator(device=device if device is not None else "cpu")
+            g.manual_seed(seed * 1000 + i * 16 + rank)
+            w = (torch.randn(m, k, generator=g, device=device) * sigma).to(dtype)
+            cls = ColumnParallelZipLinear if col else RowParallelZipLinear
+            self.layers[name] = cls(w, gemm=gemm, compressor=compressor, group=group)
+
+    def input_shapes(self, n_tokens: int):
+        """Activation shapes each projection consumes on this rank."""
+        return {name: (n_tokens, lay.in_features) for name, lay in self.layers.items()}
+
+    def run(self, xs: dict):
+        return {name: self.layers[name](xs[name]) for name in self.layers}
