@@ -169,3 +169,21 @@ def test_gpu_zipgemm_vs_reference_kernel(zs):
     assert rel_l2(ours.double().cpu(), exact.cpu()) <= GEMM_TOL
     assert rel_l2(out_ref.double().cpu(), exact.cpu()) <= GEMM_TOL
     assert rel_l2(ours.double().cpu(), out_ref.double().cpu()) <= GEMM_TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(128000, 64, 32), (16384, 256, 256), (64, 8192, 16), (8192, 1024, 200)])
+def test_gpu_zipgemm_stream_k_segments(zs, oracle, M, K, N):
+    """Shapes whose stream-K ranges cover many output tiles per CTA (drains
+    during the run), a single 64-row tile split over every SM, and N > 128."""
+    _gemm_check(zs, oracle, M, K, N, seed=M + N)
+
+
+def test_gpu_zipgemm_deterministic(zs):
+    """The split-tile reduction sums partials in a fixed order: repeated runs
+    are bit-identical."""
+    w = gen_w(4096, 4096, 3)
+    x = torch.randn(128, 4096, device="cuda").to(torch.bfloat16)
+    c = zs.compress(w)
+    y0 = zs.zipgemm(c, x)
+    for _ in range(5):
+        assert torch.equal(zs.zipgemm(c, x).view(torch.int16), y0.view(torch.int16))

@@ -54,6 +54,13 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                  : "memory");
 }
 
+// Arrive `count` times at once.
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t count) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+                 "r"(count)
+                 : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
                      smem_u32(bar)),
@@ -67,6 +74,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 // decoders sharing the SM.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
+#ifdef ZS_WAIT_HINT
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
@@ -74,6 +82,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
         : "memory");
+#elif defined(ZS_TEST_WAIT)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+#else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+#endif
     return ok != 0;
 }
 
@@ -87,8 +112,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     // kWaitLimitCycles is ~2 s at B200 clocks.
     const long long t0 = clock64();
     for (uint32_t it = 0;; ++it) {
+#ifdef ZS_SPIN_SLEEP
+        __nanosleep(ZS_SPIN_SLEEP);
+#endif
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63) == 63) {
+            if (abort_flag && *abort_flag) return false;
+            if (clock64() - t0 > kWaitLimitCycles) {
+                if (err) atomicOr(err, kErrWaitTimeout);
+                if (abort_flag) *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// Bounded wait for warps that wait often and long (decoders waiting for data):
+// between polls the warp sleeps, so it does not take issue slots from the
+// producer and MMA warps that share its scheduler.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, unsigned* err,
+                                                volatile int* abort_flag, uint32_t sleep_ns = 128) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t it = 0;; ++it) {
+        __nanosleep(sleep_ns);
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 15) == 15) {
             if (abort_flag && *abort_flag) return false;
             if (clock64() - t0 > kWaitLimitCycles) {
                 if (err) atomicOr(err, kErrWaitTimeout);

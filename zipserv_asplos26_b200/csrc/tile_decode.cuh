@@ -226,6 +226,64 @@ __device__ __forceinline__ void decode_gt_half_regs(const GtView& g, uint32_t lu
     }
 }
 
+// Decode median tile w (16 rows x 64 columns = 16 small tiles) of a staged GT
+// into 16 consecutive rows of a 128-byte-row bf16 tile in the UMMA canonical
+// 128-byte-swizzle layout (16-byte chunk c of tile row m at (c ^ (m & 7)) * 16).
+// `rows` is the tile address of the median tile's first row (a multiple of 8
+// rows into the tile).
+//
+// Lane L owns small tile s = L & 15 (column block kc = s / 2, row block
+// mr = s % 2) and rows 4 * (L >> 4) .. +3 of it. The hf offset of each small
+// tile is the median-tile base plus an exclusive scan of the small-tile hf
+// counts over the 16 lanes of the tile (ST order s = 2 kc + mr, csrc/L_API.cu
+// :623-644); the offset of a row adds the popcount of the indicator bits of
+// the rows above it. Each lane then decodes its rows with decode_row_hf and
+// finally overwrites its own fallback elements (code 0) in place, reading the
+// fallback stream in ST order.
+__device__ __forceinline__ void decode_mt_to_tile(const GtView& g, uint32_t lut_lane, const DecodeTables& t, int w,
+                                                  uint32_t rows) {
+    const int lane = threadIdx.x & 31;
+    const int s = lane & 15, rh = lane >> 4, kc = s >> 1, mr = s & 1;
+    const uint32_t st = 16u * (uint32_t)w + (uint32_t)s;
+    const uint2 v1 = lds64(g.bm + 8u * st), v2 = lds64(g.bm + g.bstride + 8u * st),
+                v3 = lds64(g.bm + 2u * g.bstride + 8u * st);
+    const uint32_t ilo = v1.x | v2.x | v3.x, ihi = v1.y | v2.y | v3.y;
+    const uint32_t plo = __popc(ilo);
+    const uint32_t hc = plo + __popc(ihi);
+    uint32_t x = hc;
+#pragma unroll
+    for (int d = 1; d < 16; d <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, d, 16);
+        if (s >= d) x += y;
+    }
+    const uint32_t excl = x - hc;
+    const uint32_t hs = lds32(g.mt + 8u * (uint32_t)w) + excl + (rh ? plo : 0u);
+    const uint32_t fs = lds32(g.mt + 8u * (uint32_t)w + 4u) + 64u * (uint32_t)s - excl + (rh ? 32u - plo : 0u);
+    const uint32_t ind = rh ? ihi : ilo;   // indicator bits of this lane's 4 rows
+    const uint32_t w1 = rh ? v1.y : v1.x, w2 = rh ? v2.y : v2.x, w3 = rh ? v3.y : v3.x;
+    const uint32_t base = rows + 128u * (8u * (uint32_t)mr + 4u * (uint32_t)rh);
+    const uint32_t sw = (uint32_t)kc ^ (4u * (uint32_t)rh);   // swizzled chunk of row r is sw ^ r
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const uint32_t sel8 = 0x4440u | (uint32_t)r;
+        const uint32_t c1 = prmt(w1, 0, sel8), c2 = prmt(w2, 0, sel8), c3 = prmt(w3, 0, sel8);
+        const uint32_t pre = r ? (uint32_t)__popc(ind & ((1u << (8 * r)) - 1u)) : 0u;
+        const uint32_t hf = min(hs + pre, g.hf_cap);
+        uint32_t o[4];
+        decode_row_hf(c1, c2, c3, lut_lane, g.sm + hf, t, o);
+        sts128(base + 128u * (uint32_t)r + ((sw ^ (uint32_t)r) << 4), o[0], o[1], o[2], o[3]);
+    }
+    uint32_t fm = ~ind;
+    uint32_t f = fs;
+    while (fm) {
+        const uint32_t j = __ffs(fm) - 1;
+        fm &= fm - 1;
+        const uint32_t r = j >> 3, c = j & 7;
+        sts16(base + 128u * r + ((sw ^ r) << 4) + 2u * c, lds16(g.full + 2u * min(f, g.full_cap)));
+        ++f;
+    }
+}
+
 // Shared-memory footprint helpers for one staged GT.
 __host__ __device__ inline uint32_t round_up_u32(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 // Bytes reserved for a GT's hf stream: capacity plus 16 bytes of read slack
