@@ -8,11 +8,13 @@
 // Behavioural notes (differences are strictly additive):
 //  * Inputs are validated on the host; bad shapes, null or misaligned pointers
 //    return cudaErrorInvalidValue instead of launching.
-//  * BF16TripleBitmap_MM_API reduces split-K partials inside the kernel (thread
-//    block cluster + distributed shared memory); Reduction_Workspace is not used
-//    and may be nullptr. Split_K >= 1 is a lower bound on the K split; the
-//    library may split further to fill the GPU. Results do not depend on it
-//    beyond fp32 summation order.
+//  * BF16TripleBitmap_MM_API splits K over all SMs itself (stream-K) and
+//    reduces split tiles inside the same kernel in a fixed order (deterministic
+//    fp32 sums, no bf16 rounding of partials). Reduction_Workspace is not used
+//    and may be nullptr; Split_K is accepted and ignored. The library keeps its
+//    own fp32 split-tile workspace per (device, stream), allocated on the first
+//    call on that stream (and grown for a larger shape): warm a stream up
+//    before capturing it into a CUDA graph.
 //  * All device work is ordered on `stream`; nothing synchronises the host.
 #pragma once
 #include <cuda.h>

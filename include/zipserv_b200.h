@@ -2,8 +2,9 @@
  *
  * Every function returns a cudaError_t value as int (0 = success). Pointers
  * named d_* are device pointers; `stream` is a cudaStream_t (NULL = legacy
- * default stream). Nothing here synchronises the host or allocates device
- * memory. Each entry point cites the reference interface it replaces
+ * default stream). Nothing here synchronises the host; only zs_zipgemm
+ * allocates device memory (its split-tile workspace, once per stream). Each
+ * entry point cites the reference interface it replaces
  * (paths inside the reference project).
  */
 #ifndef ZIPSERV_B200_H
@@ -62,8 +63,13 @@ int zs_decompress(void* stream, const uint8_t* d_sm, const uint16_t* d_full, con
                   unsigned* d_err);
 
 /* ZipGEMM: d_c[n*M + m] = sum_k W[m][k] * d_x[n*K + k] (bf16 in/out, fp32 accumulate).
- * Replaces csrc/L_API.cu:119 BF16TripleBitmap_MM_API (split-K reduced in-kernel;
- * split_k >= 1 is a lower bound on the K split). */
+ * Replaces csrc/L_API.cu:119 BF16TripleBitmap_MM_API. The K split is chosen by
+ * the library (stream-K over all SMs, split tiles reduced in-kernel in a fixed
+ * order); split_k must be >= 1 and is otherwise ignored. The first call on a
+ * stream allocates the library's fp32 split-tile workspace for that stream
+ * (grown, with a stream synchronisation, when a larger shape arrives); make
+ * that call outside CUDA-graph capture. d_x must be 16-byte aligned, d_c
+ * 8-byte aligned. */
 int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const uint64_t* d_b1,
                const uint64_t* d_b2, const uint64_t* d_b3, const int* d_mt_off, const int* d_gt_off,
                int max_hf, int max_full, int start_exp, const uint16_t* d_x, uint16_t* d_c, int M, int N,

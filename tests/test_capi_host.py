@@ -87,3 +87,23 @@ def test_invalid_shapes_rejected(zlib):
     z = np.zeros(8192, np.uint64)
     p = lambda x: x.ctypes.data_as(C.c_void_p)  # noqa: E731
     assert zlib.zs_encode_host(p(a), 64, 60, p(top), *([p(z)] * 9)) != 0
+
+
+def test_compress_host_wrapper_matches_oracle(oracle):
+    """The torch-facing host encoder returns the reference encoder's bytes."""
+    import numpy as np
+    import torch
+
+    import zipserv_asplos26_b200 as zs
+    rng = np.random.default_rng(3)
+    w = torch.from_numpy(rng.standard_normal((128, 192), dtype=np.float32) * 0.02).to(torch.bfloat16)
+    c = zs.compress_host(w)
+    e = oracle.encode(w.view(torch.int16).numpy().view(np.uint16))
+    assert c.start_exp == e.start_exp
+    assert np.array_equal(c.sign_mantissa.numpy()[: e.total_hf], e.sign_mantissa[: e.total_hf])
+    assert np.array_equal(c.compressed_full.view(torch.int16).numpy().view(np.uint16)[: e.total_full],
+                          e.full[: e.total_full])
+    for a, b in ((c.bitmap1, e.bitmap1), (c.bitmap2, e.bitmap2), (c.bitmap3, e.bitmap3)):
+        assert np.array_equal(a.numpy().view(np.uint64), b)
+    assert np.array_equal(c.tile_offsets_median.numpy(), e.mt_offsets)
+    assert np.array_equal(c.tile_offsets_global.numpy(), e.gt_offsets)

@@ -132,6 +132,54 @@ def compress(w: torch.Tensor, rule: str = "host", top: Optional[torch.Tensor] = 
                       (topl[0] - 1) & 0xFF, thf, tfull, topl)
 
 
+def compress_host(w: torch.Tensor, rule: str = "host") -> Compressed:
+    """Compress a 2-D bf16 CPU tensor with the library's multi-threaded host
+    encoder (csrc/L_API.cu:559 InitBF16MatrixTripleBitmap_Reuse semantics,
+    byte-identical to the GPU encoder); the result's tensors live on the CPU,
+    trimmed to their valid lengths."""
+    if w.is_cuda or w.dtype != torch.bfloat16 or w.dim() != 2:
+        raise ValueError("w must be a 2-D bfloat16 CPU tensor")
+    w = w.contiguous()
+    M, K = w.shape
+    if M % 64 or K % 64:
+        raise ValueError("rows and cols must be multiples of 64")
+    L = lib()
+    ngt = (M // 64) * (K // 64)
+    nst = M * K // 64
+    nmt = nst // 16
+    top = torch.empty(7, dtype=torch.int32)
+    check(L.zs_analyze_exponents_host(w.data_ptr(), w.numel(), RULES[rule], top.data_ptr()),
+          "zs_analyze_exponents_host")
+    sm = torch.empty(M * K + 16 * ngt, dtype=torch.uint8)
+    full = torch.empty(M * K + 8 * ngt, dtype=torch.bfloat16)
+    b = [torch.empty(nst, dtype=torch.uint64) for _ in range(3)]
+    st = torch.empty(2 * nst, dtype=torch.int32)
+    mt = torch.empty(2 * nmt, dtype=torch.int32)
+    gt = torch.empty(2 * (ngt + 1), dtype=torch.int32)
+    scal = torch.empty(4, dtype=torch.int32)
+    check(L.zs_encode_host(w.data_ptr(), M, K, top.data_ptr(), sm.data_ptr(), full.data_ptr(), b[0].data_ptr(),
+                           b[1].data_ptr(), b[2].data_ptr(), st.data_ptr(), mt.data_ptr(), gt.data_ptr(),
+                           scal.data_ptr()), "zs_encode_host")
+    max_hf, max_full, thf, tfull = scal.tolist()
+    topl = top.tolist()
+    return Compressed(sm[: max(thf, 16)].clone(), full[: max(tfull, 8)].clone(), b[0], b[1], b[2], st, mt, gt, M,
+                      K, max_hf, max_full, (topl[0] - 1) & 0xFF, thf, tfull, topl)
+
+
+def to_device(c: Compressed, device) -> Compressed:
+    """Copy a compressed matrix's arrays to `device` (the streams keep 16 bytes of
+    read slack past their valid length, as the GPU encoder's buffers do)."""
+    def pad(t, extra):
+        out = torch.zeros(t.numel() + extra, dtype=t.dtype)
+        out[: t.numel()] = t
+        return out.to(device)
+    return Compressed(pad(c.sign_mantissa, 16), pad(c.compressed_full, 8), c.bitmap1.to(device),
+                      c.bitmap2.to(device), c.bitmap3.to(device),
+                      None if c.tile_offsets is None else c.tile_offsets.to(device),
+                      c.tile_offsets_median.to(device), c.tile_offsets_global.to(device), c.rows, c.cols,
+                      c.max_high_freq_count, c.max_full_count, c.start_exp, c.total_hf, c.total_full, list(c.top))
+
+
 def decompress(c: Compressed, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     if out is None:
         out = torch.empty(c.rows, c.cols, dtype=torch.bfloat16, device=c.bitmap1.device)

@@ -924,7 +924,10 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const uint8_t* sm, const uint16_
     p.sm = sm; p.full = full; p.b1 = b1; p.b2 = b2; p.b3 = b3; p.mt_off = mt_off; p.gt_off = gt_off;
     p.start_exp = start_exp & 0xFF;
     p.M = M; p.K = K; p.err = err;
+#ifdef ZS_TRACE
+    // diagnostic builds: ZS_DEBUG bits switch off parts of the pipeline for timing experiments
     if (const char* d = getenv("ZS_DEBUG")) p.debug = atoi(d);
+#endif
     // N > 256 runs as column chunks of 256 (each re-decodes W; such N are
     // tensor-bound, so the repeated decode is a small share of the time)
     for (int n0 = 0; n0 < N; n0 += 256) {
