@@ -148,6 +148,13 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
     }
 }
 
+// ------------------- programmatic dependent launch -------------------------
+// Wait until the preceding grid on the stream (launched before this one) has
+// completed and its memory operations are visible. A no-op without PDL.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next grid on the stream to start launching its CTAs.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------- bulk copies (TMA engine) ------------------------
 // 1-D bulk copy global -> shared (this CTA), completion counted on `bar`.
 // Both addresses 16-byte aligned, size a multiple of 16.

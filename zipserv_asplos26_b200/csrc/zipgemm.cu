@@ -17,9 +17,10 @@
 // bf16 directly, partial segments are written as fp32 partial tiles to a
 // workspace and reduced at the end by the tile's contributing CTAs, each
 // summing a slice of the columns over the contributors in CTA order (a fixed
-// order, so results are deterministic). The CTAs of one grid are co-resident
-// (cooperative launch), which makes the end-of-kernel wait on the other
-// contributors safe.
+// order, so results are deterministic). The grid never exceeds one CTA per SM,
+// so the CTAs of a grid are co-resident and the end-of-kernel wait on the other
+// contributors is safe. Consecutive GEMMs overlap through programmatic
+// dependent launch (only X, C and the workspace wait for the previous grid).
 //
 // Inside a CTA (896 threads):
 //   warps 24, 27 compressed producers (alternate chunks): per unit, 1-D bulk copies of both GTs'
@@ -389,6 +390,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp == kBWarp) {
         if (lane == 0) {
+            // X is the previous kernel's output in a layer pipeline: wait for it
+            // (weights, decoding and the MMA ring setup do not depend on it)
+            grid_dep_wait();
             Ring rb;
             rb.init(p.nb);
             int kb = R.off0;
@@ -471,6 +475,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int sd = 0;
         int dpos = 3 * ((R.len0 + 3) / 3);
         auto drain = [&](int s) {
+            grid_dep_wait();   // C and the split-tile workspace may still be in use by the previous grid
             const int acc = s & (p.n_acc - 1);
             const long long T = R.T0 + s;
             const bool full = R.seg_full(s);
@@ -612,6 +617,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // (concurrently) until every contributor of the respective tile has
     // published its partial tile; then the CTA sums its slice of the columns of
     // each such tile over the contributors in CTA order and writes bf16.
+    if (tid == 0) grid_dep_launch();   // the next grid may start on SMs this grid frees
+    grid_dep_wait();                   // C and the workspace may still be in use by the previous grid
     const long long U = p.units;
     long long fT[2] = {-1, -1}, fcf[2] = {0, 0};
     int fn[2] = {0, 0}, fidx[2] = {0, 0}, fslot0[2] = {0, 0};
@@ -893,8 +900,14 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, int dev,
     p.smem_bytes = smem_bytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
+    // Programmatic dependent launch: this grid's CTAs may start (prologue,
+    // weight loads, decoding) while the previous grid on the stream finishes;
+    // the kernel waits on it (griddepcontrol.wait) before reading X and before
+    // touching C and the workspace. All CTAs of a grid are resident at once
+    // (G <= #SMs, one CTA per SM) and a grid never waits on a later one, so the
+    // split-tile wait cannot deadlock.
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, zipgemm_kernel, maps, p);
