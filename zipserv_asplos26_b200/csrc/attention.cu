@@ -34,11 +34,14 @@ namespace zs {
 
 constexpr int kAttnMaxG = 8;        // query heads per KV head
 constexpr int kAttnD = 128;         // head dim (two 64-wide GTs)
-constexpr int kAttnWarps = 9;
+constexpr int kAttnDecWarps = 16;   // one median-tile task of K or V per page each
+constexpr int kAttnProducer = 16;
+constexpr int kAttnMath0 = 17;      // math warps 17 and 18 take alternate pages
+constexpr int kAttnWarps = 19;
 constexpr int kAttnThreads = 32 * kAttnWarps;
-constexpr int kAttnProducer = 8;
-constexpr int kAttnMaxChunk = 4;    // pages per compressed slot
-constexpr int kAttnSlots = 3;
+constexpr int kAttnSlots = 3;       // compressed pages (K + V) in flight
+constexpr int kAttnTiles = 3;       // decoded pages: K 16 KB + V 16 KB each
+constexpr uint32_t kAttnTileBytes = 32768;
 
 struct AttnStream {
     const uint8_t* sm;
@@ -57,72 +60,69 @@ struct AttnParams {
     const int* seqlens;       // [B]
     uint16_t* out;            // [B][Hq][D] bf16
     float* ws;                // [B*Hkv][S][G][D + 2] fp32 when S > 1
-    int B, Hq, Hkv, G, T_pad, S, pages_per_split, chunk;
+    int B, Hq, Hkv, G, T_pad, S, pages_per_split;
     float scale_log2;         // softmax_scale * log2(e)
-    // compressed slot layout (bytes), per stream (K at 0, V at c_stream)
-    uint32_t c_stream, c_mt, c_hf, c_full, hf_cap, full_cap, c_slot;
+    // compressed page slot: per matrix (K at 0, V at c_mat):
+    //   [b1 | b2 | b3: 2 GTs x 512 B each] [mt: 2 x 32 B] [hf: 2 GTs] [fallback: 2 GTs]
+    uint32_t c_mat, c_hf, c_full, hf_cap, full_cap, c_slot;
+    uint32_t off_tiles, off_slots;
+    int nslots;               // depth of the page rings (compressed slots and decoded tiles): 3, or 2 for large streams
     unsigned* err;
 };
 
 struct AttnSmem {
-    uint64_t full[kAttnSlots], empty[kAttnSlots];
+    uint64_t cfull[kAttnSlots], cempty[kAttnSlots];
+    uint64_t tfull[kAttnTiles], tempty[kAttnTiles];
     int abort_flag;
-    // per slot and stream: GT-local stream offsets of each GT of the chunk
-    int hoff[kAttnSlots][2][2 * kAttnMaxChunk + 1];
-    int foff[kAttnSlots][2][2 * kAttnMaxChunk + 1];
-    __align__(16) float q[kAttnMaxG][kAttnD];   // query heads of this KV head, fp32 (read as float2)
-    float sc[2][kAttnMaxG][64];            // partial scores from the two 64-dim halves
-    float p[64][kAttnMaxG];                // softmax weights of the current page
-    float alpha[kAttnMaxG];                // rescale of the running output
-    __align__(16) uint16_t v[64][kAttnD + 8];   // decoded V page (+16 B row pad)
+    int2 info[kAttnSlots][2];          // per slot and matrix: stream offsets of the page's second GT
+    float mo[kAttnMaxG][kAttnD];       // second math warp's partial output (final merge)
+    __align__(16) uint16_t qs[kAttnMaxG][kAttnD + 8];   // query heads (bf16), rows padded against bank conflicts
+    float mm[kAttnMaxG], ml[kAttnMaxG];
 };
 
-static_assert(offsetof(AttnSmem, q) % 16 == 0 && offsetof(AttnSmem, v) % 16 == 0, "vector-accessed members");
-
-// Barrier over the 8 compute warps only (the producer warp never joins).
-__device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-
-// One producer step: copy `np` pages starting at page `pg` of row block `rb`
-// (= (b * Hkv + h) * T_pad / 64) of one stream into the slot.
-__device__ __forceinline__ uint32_t attn_issue_stream(const AttnStream& s, uint8_t* dst, long long gt0, int ngt,
-                                                      int* hoff, int* foff, const AttnParams& p, uint64_t* bar,
-                                                      bool issue) {
-    const int2* go = reinterpret_cast<const int2*>(s.gt_off) + gt0;
-    const int2 a0 = go[0];
-    for (int i = 0; i <= ngt; ++i) {
-        const int2 a = go[i];
-        hoff[i] = a.x - a0.x;
-        foff[i] = a.y - a0.y;
-    }
-    const int2 a1 = go[ngt];
-    uint32_t hb = a1.x > a0.x ? (uint32_t)(a1.x - a0.x) : 0u;
-    uint32_t fb = a1.y > a0.y ? (uint32_t)(a1.y - a0.y) * 2u : 0u;
-    int h0 = a0.x, f0 = a0.y;
-    if (hb > p.hf_cap || fb > p.full_cap || (hb & 15u) || (fb & 15u) || (h0 & 15) || (f0 & 7) || h0 < 0 || f0 < 0) {
-        if (p.err) atomicOr(p.err, kErrStreamOverflow);
-        hb = min(hb, p.hf_cap) & ~15u;
-        fb = min(fb, p.full_cap) & ~15u;
-        h0 = max(h0, 0) & ~15;
-        f0 = max(f0, 0) & ~7;
-    }
-    const uint32_t bytes = (uint32_t)ngt * (3 * 512 + 32) + hb + fb;
-    if (issue) {
-        const uint32_t bmb = 512u * (uint32_t)ngt;
-        bulk_g2s(dst, s.b1 + gt0 * 64, bmb, bar);
-        bulk_g2s(dst + 512u * 2 * p.chunk, s.b2 + gt0 * 64, bmb, bar);
-        bulk_g2s(dst + 1024u * 2 * p.chunk, s.b3 + gt0 * 64, bmb, bar);
-        bulk_g2s(dst + p.c_mt, s.mt_off + gt0 * 8, 32u * (uint32_t)ngt, bar);
-        if (hb) bulk_g2s(dst + p.c_hf, s.sm + h0, hb, bar);
-        if (fb) bulk_g2s(dst + p.c_full, s.full + f0, fb, bar);
-    }
-    return bytes;
+// ---------------- legacy tensor-core helpers for the small attention math ----------------
+// (G <= 8 query heads per page: far too small for tcgen05 tiles; mma.sync m16n8k16 with the
+// heads in rows 0..7 and ldmatrix from the decoded, 128-byte-swizzled page tiles.)
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+// d[0..1] += A(rows 0-7: a0 / a2, rows 8-15 zero) * B; the zero rows' results are dropped.
+__device__ __forceinline__ void mma_rows8(float& d0, float& d1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    float x2, x3;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %10, %10};"
+        : "+f"(d0), "+f"(d1), "=f"(x2), "=f"(x3)
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(0.f));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// Kernel: one CTA per (b, kv head, split) works through its pages:
+//   warp 16      producer: per page, lanes 0-11 bulk-copy the six streams of the
+//                two GTs of K and of V (one warp instruction); GT offsets are
+//                fetched one page ahead
+//   warps 0-15   decoders: warp w always decodes median tile w % 4 of GT (w / 4) % 2
+//                of K (w < 8) or V into the page's 128-byte-swizzled bf16 tiles
+//   warps 17-18  math on alternate pages: S = Q K^T and O += P V with mma.sync
+//                (K fragments by ldmatrix, V by ldmatrix.trans; P reuses the S
+//                accumulator registers as the A operand), online base-2 softmax
+// The two math warps merge (m, l, O) at the end; with S > 1 splits the CTA writes
+// (m, l, unnormalised O) to the workspace for attn_combine_kernel.
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const AttnParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     AttnSmem& A = *reinterpret_cast<AttnSmem*>(smem);
     uint32_t* lut = reinterpret_cast<uint32_t*>(smem + round_up_u32(sizeof(AttnSmem), 1024));
-    uint8_t* slots = reinterpret_cast<uint8_t*>(lut + kLutWords);
+    const uint32_t smem0 = smem_u32(smem);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh = blockIdx.x, split = blockIdx.y;
@@ -135,185 +135,259 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
     const long long rb = ((long long)bh * p.T_pad) >> 6;   // first GT row of this (b, kv head)
 
     fill_spread_table(lut, tid, kAttnThreads);
-    for (int i = tid; i < G * kAttnD; i += kAttnThreads) {
+    for (int i = tid; i < kAttnMaxG * kAttnD; i += kAttnThreads) {
         const int h = i / kAttnD, d = i % kAttnD;
-        A.q[h][d] = __uint_as_float((uint32_t)p.q[((size_t)b * p.Hq + hk * G + h) * kAttnD + d] << 16);
+        A.qs[h][d] = h < G ? p.q[((size_t)b * p.Hq + hk * G + h) * kAttnD + d] : (uint16_t)0;
     }
     if (tid == 0) {
-        for (int s = 0; s < kAttnSlots; ++s) { mbar_init(&A.full[s], 1); mbar_init(&A.empty[s], 8); }
+        for (int s = 0; s < p.nslots; ++s) {
+            mbar_init(&A.cfull[s], 1);
+            mbar_init(&A.cempty[s], kAttnDecWarps);
+            mbar_init(&A.tfull[s], kAttnDecWarps);
+            mbar_init(&A.tempty[s], 1);
+        }
         A.abort_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
     volatile int* abort_flag = &A.abort_flag;
-    const int nchunks = (np + p.chunk - 1) / p.chunk;
-
-    // per-lane online-softmax state (warp h < G owns head h) and P.V accumulators
-    float m_run = -INFINITY, l_run = 0.f;
-    const int dp = tid & 63, tq = (tid >> 6) & 3;   // P.V: dims 2dp, 2dp+1; tokens 16tq..16tq+15
-    float acc[kAttnMaxG][2];
-#pragma unroll
-    for (int h = 0; h < kAttnMaxG; ++h) acc[h][0] = acc[h][1] = 0.f;
 
     if (warp == kAttnProducer) {
-        if (lane == 0) {
-            for (int j = 0; j < nchunks; ++j) {
-                const int s = j % kAttnSlots;
-                if (j >= kAttnSlots && !mbar_wait(&A.empty[s], ((j / kAttnSlots) + 1) & 1, p.err, abort_flag)) break;
-                const int pj = pg0 + j * p.chunk, cn = min(p.chunk, np - j * p.chunk);
-                const long long gt0 = (rb + pj) * 2;
-                uint8_t* slot = slots + (size_t)s * p.c_slot;
-                uint32_t bytes = attn_issue_stream(p.k, slot, gt0, 2 * cn, A.hoff[s][0], A.foff[s][0], p, nullptr, false) +
-                                 attn_issue_stream(p.v, slot + p.c_stream, gt0, 2 * cn, A.hoff[s][1], A.foff[s][1], p,
-                                                   nullptr, false);
-                mbar_arrive_expect_tx(&A.full[s], bytes);
-                attn_issue_stream(p.k, slot, gt0, 2 * cn, A.hoff[s][0], A.foff[s][0], p, &A.full[s], true);
-                attn_issue_stream(p.v, slot + p.c_stream, gt0, 2 * cn, A.hoff[s][1], A.foff[s][1], p, &A.full[s],
-                                  true);
-            }
-        }
-        // The producer takes no part in the compute-warp barriers below; its
-        // copies complete on the slot barriers the compute warps wait on.
-        return;
-    }
-
-    const DecodeTables tk = make_decode_tables(p.k.start_exp), tv = make_decode_tables(p.v.start_exp);
-    const uint32_t lut_lane = launder(smem_u32(lut)) + 4u * (uint32_t)lane;
-    for (int pi = 0; pi < np; ++pi) {
-        const int j = pi / p.chunk, u = pi - j * p.chunk, s = j % kAttnSlots;
-        const int tok0 = (pg0 + pi) * 64;
-        const bool ok = mbar_wait(&A.full[s], (j / kAttnSlots) & 1, p.err, abort_flag);
-        if (ok) {
-            const int isv = warp >> 2, sub = (warp >> 1) & 1, half = warp & 1;
-            const uint32_t base = launder(smem_u32(slots + (size_t)s * p.c_slot + isv * p.c_stream));
-            const int gi = 2 * u + sub;
-            GtView g;
-            g.bm = base + 512u * (uint32_t)gi;
-            g.bstride = 512u * 2u * (uint32_t)p.chunk;
-            g.mt = base + p.c_mt + 32u * (uint32_t)gi;
-            const uint32_t hl = (uint32_t)min(max(A.hoff[s][isv][gi], 0), (int)p.hf_cap);
-            const uint32_t fl = (uint32_t)min(max(A.foff[s][isv][gi], 0) * 2, (int)p.full_cap);
-            g.sm = base + p.c_hf + hl;
-            g.full = base + p.c_full + fl;
-            g.hf_cap = p.hf_cap - hl;
-            g.full_cap = (p.full_cap - fl) / 2;
-            const int t = 32 * half + lane;   // token within the page
-            if (isv == 0) {
-                float dot[kAttnMaxG];
-#pragma unroll
-                for (int h = 0; h < kAttnMaxG; ++h) dot[h] = 0.f;
-                decode_gt_half_regs<8>(g, lut_lane, tk, half, 0,
-                                       [&](int kc, uint32_t o0, uint32_t o1, uint32_t o2, uint32_t o3) {
-                                           const uint32_t ow[4] = {o0, o1, o2, o3};
-                                           const int d0 = sub * 64 + kc * 8;
-#pragma unroll
-                                           for (int e = 0; e < 4; ++e) {
-                                               const float k0 = __uint_as_float(ow[e] << 16);
-                                               const float k1 = __uint_as_float(ow[e] & 0xFFFF0000u);
-#pragma unroll
-                                               for (int h = 0; h < kAttnMaxG; ++h)
-                                                   if (h < G) {
-                                                       const float2 qq = *reinterpret_cast<const float2*>(
-                                                           &A.q[h][d0 + 2 * e]);
-                                                       dot[h] = fmaf(k0, qq.x, fmaf(k1, qq.y, dot[h]));
-                                                   }
-                                           }
-                                       });
-#pragma unroll
-                for (int h = 0; h < kAttnMaxG; ++h)
-                    if (h < G) A.sc[sub][h][t] = dot[h];
-            } else {
-                decode_gt_half_regs<8>(g, lut_lane, tv, half, 0,
-                                       [&](int kc, uint32_t o0, uint32_t o1, uint32_t o2, uint32_t o3) {
-                                           *reinterpret_cast<uint4*>(&A.v[t][sub * 64 + kc * 8]) =
-                                               make_uint4(o0, o1, o2, o3);
-                                       });
-            }
-        }
-        compute_sync();
-        // the slot holds a chunk of pages: release it after the chunk's last page
-        if (lane == 0 && (u == p.chunk - 1 || pi == np - 1)) mbar_arrive(&A.empty[s]);
-        // online softmax: warp h owns query head h, lanes own tokens lane, lane + 32
-        if (warp < G) {
-            const int h = warp;
-            float s0 = (A.sc[0][h][lane] + A.sc[1][h][lane]) * p.scale_log2;
-            float s1 = (A.sc[0][h][lane + 32] + A.sc[1][h][lane + 32]) * p.scale_log2;
-            if (tok0 + lane >= len) s0 = -INFINITY;
-            if (tok0 + lane + 32 >= len) s1 = -INFINITY;
-            float mx = fmaxf(s0, s1);
-            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-            const float m_new = fmaxf(m_run, mx);
-            const float e0 = exp2f(s0 - m_new), e1 = exp2f(s1 - m_new);
-            float sum = e0 + e1;
-            for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-            const float al = exp2f(m_run - m_new);   // 0 on the first page (m_run = -inf)
-            l_run = l_run * al + sum;
-            m_run = m_new;
-            A.p[lane][h] = e0;
-            A.p[lane + 32][h] = e1;
-            if (lane == 0) A.alpha[h] = al;
-        }
-        compute_sync();
-        {
-#pragma unroll
-            for (int h = 0; h < kAttnMaxG; ++h)
-                if (h < G) {
-                    const float al = A.alpha[h];
-                    acc[h][0] *= al;
-                    acc[h][1] *= al;
-                }
-#pragma unroll 4
-            for (int tt = 0; tt < 16; ++tt) {
-                const int t = tq * 16 + tt;
-                const uint32_t vv = *reinterpret_cast<const uint32_t*>(&A.v[t][2 * dp]);
-                const float v0 = __uint_as_float(vv << 16), v1 = __uint_as_float(vv & 0xFFFF0000u);
-#pragma unroll
-                for (int h = 0; h < kAttnMaxG; ++h)
-                    if (h < G) {
-                        const float pp = A.p[t][h];
-                        acc[h][0] = fmaf(pp, v0, acc[h][0]);
-                        acc[h][1] = fmaf(pp, v1, acc[h][1]);
+        // lanes 0-5: K streams (b1, b2, b3, mt, hf, fallback), lanes 6-11: V streams;
+        // lanes 0-2 / 3-5 hold the K / V GT offsets of GTs 2r, 2r+1, 2r+2 of the page
+        const int mat = lane / 6, kind = lane % 6;
+        const AttnStream& S = mat ? p.v : p.k;
+        const AttnStream& So = lane < 3 ? p.k : p.v;
+        auto fetch = [&](int pi) {
+            int2 e = make_int2(0, 0);
+            if (pi < np && lane < 6) e = reinterpret_cast<const int2*>(So.gt_off)[(rb + pg0 + pi) * 2 + (lane % 3)];
+            return e;
+        };
+        int2 cur = fetch(0);
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int pi = 0; pi < np && ok; ++pi) {
+            const int2 nxt = fetch(pi + 1);   // in flight while this page is issued
+            if (lane == 0 && pi >= p.nslots) ok = mbar_wait(&A.cempty[s], ph ^ 1u, p.err, abort_flag);
+            ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            const int mb = 3 * mat;
+            const int h0 = __shfl_sync(0xFFFFFFFFu, cur.x, mb), f0 = __shfl_sync(0xFFFFFFFFu, cur.y, mb);
+            const int h1 = __shfl_sync(0xFFFFFFFFu, cur.x, mb + 1), f1 = __shfl_sync(0xFFFFFFFFu, cur.y, mb + 1);
+            const int h2 = __shfl_sync(0xFFFFFFFFu, cur.x, mb + 2), f2 = __shfl_sync(0xFFFFFFFFu, cur.y, mb + 2);
+            uint8_t* slot = smem + p.off_slots + (size_t)s * p.c_slot + (size_t)mat * p.c_mat;
+            const long long gt0 = (rb + pg0 + pi) * 2;
+            uint32_t size = 0, dst = 0;
+            const void* src = nullptr;
+            if (lane < 12) {
+                if (kind < 3) {
+                    size = 1024u;
+                    dst = 1024u * (uint32_t)kind;
+                    src = (kind == 0 ? S.b1 : (kind == 1 ? S.b2 : S.b3)) + gt0 * 64;
+                } else if (kind == 3) {
+                    size = 64u;
+                    dst = 3072u;
+                    src = S.mt_off + gt0 * 8;
+                } else {
+                    const bool hf = kind == 4;
+                    const int beg = hf ? h0 : f0, end = hf ? h2 : f2;
+                    const uint32_t esz = hf ? 1u : 2u, cap = hf ? p.hf_cap : p.full_cap;
+                    const int al = hf ? 16 : 8;
+                    uint32_t bytes = end > beg ? (uint32_t)(end - beg) * esz : 0u;
+                    int bg = beg;
+                    if (bytes > cap || (bytes & 15u) || (bg & (al - 1)) || bg < 0) {
+                        if (p.err) atomicOr(p.err, kErrStreamOverflow);
+                        bytes = min(bytes, cap) & ~15u;
+                        bg = max(bg, 0) & ~(al - 1);
                     }
+                    size = bytes;
+                    dst = hf ? p.c_hf : p.c_full;
+                    src = hf ? (const void*)(S.sm + bg) : (const void*)(S.full + bg);
+                }
+            }
+            if (lane == 0 || lane == 6)
+                A.info[s][mat] = make_int2(max(h1 - h0, 0), max(f1 - f0, 0));
+            const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, size);
+            __syncwarp();   // the page's offsets above are released by lane 0's arrive
+            if (lane == 0) mbar_arrive_expect_tx(&A.cfull[s], total);
+            __syncwarp();
+            if (size) bulk_g2s(slot + dst, src, size, &A.cfull[s]);
+            cur = nxt;
+            if (++s == p.nslots) { s = 0; ph ^= 1u; }
+        }
+    } else if (warp < kAttnDecWarps) {
+        const int mat = warp >> 3, gc = (warp >> 2) & 1, mtile = warp & 3;
+        const DecodeTables tabs = make_decode_tables(mat ? p.v.start_exp : p.k.start_exp);
+        const uint32_t lut_lane = launder(smem_u32(lut)) + 4u * (uint32_t)lane;
+        int s = 0;
+        uint32_t ph = 0;
+        for (int pi = 0; pi < np; ++pi) {
+            if (*abort_flag) break;
+            if (!mbar_wait_sleep(&A.cfull[s], ph, p.err, abort_flag)) break;
+            if (pi >= p.nslots && !mbar_wait_sleep(&A.tempty[s], ph ^ 1u, p.err, abort_flag)) break;
+            const uint32_t base = launder(smem0 + p.off_slots + (uint32_t)s * p.c_slot + (uint32_t)mat * p.c_mat);
+            const int2 inf = gc ? A.info[s][mat] : make_int2(0, 0);
+            const uint32_t h0 = min((uint32_t)inf.x, p.hf_cap), f0 = min((uint32_t)inf.y, p.full_cap / 2);
+            GtView g;
+            g.bm = base + 512u * (uint32_t)gc;
+            g.bstride = 1024u;
+            g.mt = base + 3072u + 32u * (uint32_t)gc;
+            g.sm = base + p.c_hf + h0;
+            g.full = base + p.c_full + 2u * f0;
+            g.hf_cap = p.hf_cap - h0;
+            g.full_cap = p.full_cap / 2 - f0;
+            const uint32_t rows = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes + 16384u * (uint32_t)mat +
+                                  8192u * (uint32_t)gc + 2048u * (uint32_t)mtile;
+            decode_mt_to_tile(g, lut_lane, tabs, mtile, rows);
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&A.tfull[s]);
+                mbar_arrive(&A.cempty[s]);
+            }
+            if (++s == p.nslots) { s = 0; ph ^= 1u; }
+        }
+    } else {
+        // math warps: rows of the mma tiles = query heads (group = lane / 4 < G)
+        const int mw = warp - kAttnMath0;
+        const int grp = lane >> 2, t4 = lane & 3;
+        float o[16][2];
+#pragma unroll
+        for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = 0.f;
+        float m_run = -INFINITY, l_run = 0.f;
+        int s = mw % p.nslots, kround = mw / p.nslots;   // page pi = mw + 2j: tile slot pi % n, round pi / n
+        for (int pi = mw; pi < np; pi += 2) {
+            if (!mbar_wait(&A.tfull[s], (uint32_t)(kround & 1), p.err, abort_flag)) break;
+            const uint32_t kt = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes, vt = kt + 16384u;
+            // S = Q K^T over the page's 64 tokens (8 n-tiles of 8 tokens)
+            float sc[8][2];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = 0.f;
+            const int mi = lane >> 3, rr = lane & 7;
+            // lane's row address in the Q tile for ldmatrix: matrix mi = (k-step 2 k2 + mi / 2, dims half mi % 2)
+            const uint32_t qbase = smem_u32(&A.qs[rr][0]) + 16u * (uint32_t)mi;
+#pragma unroll
+            for (int jp = 0; jp < 4; ++jp) {
+                const uint32_t tok = 8u * (uint32_t)(2 * jp + (mi >> 1)) + (uint32_t)rr;
+#pragma unroll
+                for (int k2 = 0; k2 < 4; ++k2) {
+                    // Q A-fragments of k-steps 2 k2 and 2 k2 + 1 (rows 0-7 = query heads)
+                    uint32_t q0, q1, q2, q3;
+                    ldsm_x4(qbase + 64u * (uint32_t)k2, q0, q1, q2, q3);
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        const int kk = 2 * k2 + h2;
+                        const uint32_t chunk = 2u * (uint32_t)(kk & 3) + (uint32_t)(mi & 1);
+                        const uint32_t addr =
+                            kt + 8192u * (uint32_t)(kk >> 2) + tok * 128u + ((chunk ^ (tok & 7u)) << 4);
+                        uint32_t b0, b1, b2, b3;
+                        ldsm_x4(addr, b0, b1, b2, b3);
+                        const uint32_t a0 = h2 ? q2 : q0, a2 = h2 ? q3 : q1;
+                        mma_rows8(sc[2 * jp][0], sc[2 * jp][1], a0, a2, b0, b1);
+                        mma_rows8(sc[2 * jp + 1][0], sc[2 * jp + 1][1], a0, a2, b2, b3);
+                    }
+                }
+            }
+            // online softmax of row grp (tokens 8j + 2 t4 + e of this page)
+            const int tok0 = (pg0 + pi) * 64;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int t = tok0 + 8 * j + 2 * t4 + e;
+                    const float x = t < len ? sc[j][e] * p.scale_log2 : -INFINITY;
+                    sc[j][e] = x;
+                    mx = fmaxf(mx, x);
+                }
+            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+            const float m_new = fmaxf(m_run, mx);
+            const float mref = m_new == -INFINITY ? 0.f : m_new;
+            const float alpha = exp2f(m_run - mref);
+            float sum = 0.f;
+            // P as a bf16 pair hi + lo (lo = the rounding residual) so that P.V keeps
+            // ~16 bits of P: two mma per fragment instead of one
+            uint32_t pa0[4], pa2[4], pl0[4], pl2[4];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float e0 = exp2f(sc[j][0] - mref), e1 = exp2f(sc[j][1] - mref);
+                sum += e0 + e1;
+                const __nv_bfloat162 hi = __floats2bfloat162_rn(e0, e1);
+                const float2 hf = __bfloat1622float2(hi);
+                const uint32_t h = *reinterpret_cast<const uint32_t*>(&hi), l = pack_bf16(e0 - hf.x, e1 - hf.y);
+                if (j & 1) { pa2[j >> 1] = h; pl2[j >> 1] = l; }
+                else { pa0[j >> 1] = h; pl0[j >> 1] = l; }
+            }
+            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+            l_run = l_run * alpha + sum;
+            m_run = m_new;
+#pragma unroll
+            for (int n = 0; n < 16; ++n) {
+                o[n][0] *= alpha;
+                o[n][1] *= alpha;
+            }
+            // O += P V: 16 n-tiles of 8 dims, 4 k-steps of 16 tokens
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t tok = 16u * (uint32_t)kk + 8u * (uint32_t)(mi & 1) + (uint32_t)rr;
+#pragma unroll
+                for (int np2 = 0; np2 < 8; ++np2) {
+                    const uint32_t dc = 2u * (uint32_t)np2 + (uint32_t)(mi >> 1);   // 8-dim chunk 0..15
+                    const uint32_t addr = vt + 8192u * (dc >> 3) + tok * 128u + (((dc & 7u) ^ (tok & 7u)) << 4);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(addr, b0, b1, b2, b3);
+                    mma_rows8(o[2 * np2][0], o[2 * np2][1], pa0[kk], pa2[kk], b0, b1);
+                    mma_rows8(o[2 * np2 + 1][0], o[2 * np2 + 1][1], pa0[kk], pa2[kk], b2, b3);
+                    mma_rows8(o[2 * np2][0], o[2 * np2][1], pl0[kk], pl2[kk], b0, b1);
+                    mma_rows8(o[2 * np2 + 1][0], o[2 * np2 + 1][1], pl0[kk], pl2[kk], b2, b3);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&A.tempty[s]);
+            s += 2;
+            while (s >= p.nslots) { s -= p.nslots; ++kround; }
+        }
+        // merge the two math warps: warp 18 publishes, warp 17 combines and writes
+        if (mw == 1) {
+            if (grp < G) {
+#pragma unroll
+                for (int n = 0; n < 16; ++n) {
+                    A.mo[grp][8 * n + 2 * t4] = o[n][0];
+                    A.mo[grp][8 * n + 2 * t4 + 1] = o[n][1];
+                }
+                if (t4 == 0) { A.mm[grp] = m_run; A.ml[grp] = l_run; }
             }
         }
-        compute_sync();
-    }
-
-    // reduce the four token quarters; reuse the V tile as fp32 scratch [4][G][D]
-    float* red = reinterpret_cast<float*>(&A.v[0][0]);
-    if (tq > 0) {
-#pragma unroll
-        for (int h = 0; h < kAttnMaxG; ++h)
-            if (h < G) {
-                red[((tq - 1) * G + h) * kAttnD + 2 * dp] = acc[h][0];
-                red[((tq - 1) * G + h) * kAttnD + 2 * dp + 1] = acc[h][1];
-            }
-    }
-    if (warp < G && lane == 0) {
-        A.alpha[warp] = m_run;      // reuse: running max and sum of head h
-        A.sc[0][warp][0] = l_run;
-    }
-    compute_sync();
-    if (tq == 0) {
-        for (int h = 0; h < G; ++h) {
-            float a0 = acc[h][0], a1 = acc[h][1];
-            for (int k = 0; k < 3; ++k) {
-                a0 += red[(k * G + h) * kAttnD + 2 * dp];
-                a1 += red[(k * G + h) * kAttnD + 2 * dp + 1];
-            }
-            const float m = A.alpha[h], l = A.sc[0][h][0];
-            const int hq = hk * G + h;
+        asm volatile("bar.sync 1, 64;" ::: "memory");
+        if (mw == 0 && grp < G) {
+            const float m1 = A.mm[grp], l1 = A.ml[grp];
+            const float M = fmaxf(m_run, m1);
+            const float Mref = M == -INFINITY ? 0.f : M;
+            const float s0 = exp2f(m_run - Mref), s1 = exp2f(m1 - Mref);
+            const float L = l_run * s0 + l1 * s1;
+            const int hq = hk * G + grp;
             if (p.S == 1) {
-                const float inv = l > 0.f ? 1.f / l : 0.f;
-                __nv_bfloat162 o = __floats2bfloat162_rn(a0 * inv, a1 * inv);
-                *reinterpret_cast<__nv_bfloat162*>(&p.out[((size_t)b * p.Hq + hq) * kAttnD + 2 * dp]) = o;
+                const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+                for (int n = 0; n < 16; ++n) {
+                    const int d = 8 * n + 2 * t4;
+                    const float v0 = (o[n][0] * s0 + A.mo[grp][d] * s1) * inv;
+                    const float v1 = (o[n][1] * s0 + A.mo[grp][d + 1] * s1) * inv;
+                    *reinterpret_cast<uint32_t*>(&p.out[((size_t)b * p.Hq + hq) * kAttnD + d]) = pack_bf16(v0, v1);
+                }
             } else {
-                float* w = p.ws + (((size_t)bh * p.S + split) * G + h) * (kAttnD + 2);
-                w[2 * dp] = a0;
-                w[2 * dp + 1] = a1;
-                if (dp == 0) {
-                    w[kAttnD] = m;
-                    w[kAttnD + 1] = l;
+                float* w = p.ws + (((size_t)bh * p.S + split) * G + grp) * (kAttnD + 2);
+#pragma unroll
+                for (int n = 0; n < 16; ++n) {
+                    const int d = 8 * n + 2 * t4;
+                    w[d] = o[n][0] * s0 + A.mo[grp][d] * s1;
+                    w[d + 1] = o[n][1] * s0 + A.mo[grp][d + 1] * s1;
+                }
+                if (t4 == 0) {
+                    w[kAttnD] = M;
+                    w[kAttnD + 1] = L;
                 }
             }
         }
@@ -396,27 +470,25 @@ cudaError_t launch_attention(cudaStream_t stream, const AttnCompressed& kc, cons
     p.scale_log2 = softmax_scale * 1.4426950408889634f;
     const uint32_t hfc = round_up_u32((uint32_t)std::max(kc.max_hf, vc.max_hf), 16);
     const uint32_t ffc = round_up_u32((uint32_t)std::max(kc.max_full, vc.max_full) * 2u, 16);
-    const uint32_t head = round_up_u32(sizeof(AttnSmem), 1024) + 4u * kLutWords;
+    // compressed page slot per matrix: 3 x 1 KB bitmaps, 64 B median offsets, the
+    // two GTs' hf stream (+16 B read slack) and fallback stream
+    p.c_hf = 3072u + 64u;
+    p.hf_cap = 2u * hfc;
+    p.c_full = p.c_hf + p.hf_cap + 16u;
+    p.full_cap = 2u * ffc;
+    p.c_mat = round_up_u32(p.c_full + p.full_cap + 16u, 128);
+    p.c_slot = 2u * p.c_mat;
+    p.off_tiles = round_up_u32(round_up_u32(sizeof(AttnSmem), 1024) + 4u * kLutWords, 1024);
     int dev = 0, max_smem = 232448;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    p.chunk = 1;
-    for (int ch = kAttnMaxChunk; ch >= 1; --ch) {
-        const uint32_t ngt = 2u * ch;
-        const uint32_t stream = round_up_u32(ngt * (1536u + 32u) + ngt * hfc + 16 + ngt * ffc + 16, 128);
-        if (head + kAttnSlots * 2 * stream <= (uint32_t)max_smem) { p.chunk = ch; break; }
-    }
-    {
-        const uint32_t ngt = 2u * p.chunk;
-        p.c_mt = 1536u * ngt;
-        p.c_hf = p.c_mt + 32u * ngt;
-        p.hf_cap = hfc * ngt;
-        p.c_full = p.c_hf + p.hf_cap + 16;
-        p.full_cap = ffc * ngt;
-        p.c_stream = round_up_u32(p.c_full + p.full_cap + 16, 128);
-        p.c_slot = 2 * p.c_stream;
-    }
-    const uint32_t smem_bytes = head + kAttnSlots * p.c_slot;
+    // three pages in flight when the streams allow (large fallback streams, e.g.
+    // zero-padded pages, leave room for two)
+    p.nslots = 3;
+    while (p.nslots > 2 && p.off_tiles + (uint32_t)p.nslots * (kAttnTileBytes + p.c_slot) > (uint32_t)max_smem)
+        --p.nslots;
+    p.off_slots = p.off_tiles + (uint32_t)p.nslots * kAttnTileBytes;
+    const uint32_t smem_bytes = p.off_slots + (uint32_t)p.nslots * p.c_slot;
     if (smem_bytes > (uint32_t)max_smem) return cudaErrorInvalidValue;
     ZS_RETURN_IF_ERR(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem_bytes));

@@ -39,6 +39,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -85,7 +86,7 @@ struct GemmParams {
     long long units;
     int nb, na, nc;
     int cu;                         // units per compressed chunk (1, 2 or 4)
-    int lcu, lnc, lna, lacc;        // log2 of cu, nc, na, n_acc (all powers of two)
+    int lcu, lnc, lacc;             // log2 of cu, nc, n_acc (powers of two)
     uint32_t off_b, off_a, off_c;   // ring bases (shared-memory offsets)
     uint32_t b_slot, c_slot;
     uint32_t c_mt;                  // chunk slot: [b1 | b2 | b3] x [2 GT rows][cu][512 B], mt [2][cu][32 B],
@@ -535,6 +536,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         long long T = R.T0;
         int kb = R.off0 + i;
         while (kb >= R.gtk) { kb -= R.gtk; ++T; }
+        // A-ring slot and use count of unit i, advanced by 3 units per row (na is any size >= 2)
+        int sa = i % p.na, around = i / p.na;
         for (int g = 0; 3 * g < R.n; ++g, i += 3) {
             while (sd < mid_end && dpos == 3 * g) {
                 drain(sd);
@@ -550,7 +553,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int u = (int)(gu & cmask) - (c == 0 ? (int)(R.u0 & cmask) : 0);
                 const int start = i - u;
                 const int clen = min(p.cu - (int)((R.u0 + start) & cmask), R.n - start);
-                const int cs = c & (p.nc - 1), sa = i & (p.na - 1);
+                const int cs = c & (p.nc - 1);
 #ifdef ZS_TRACE
                 const int tq = g;
                 if (lane == 0 && (warp == 0 || warp == 13) && tq < 6) ZS_STAMP(70 + 4 * tq + (warp ? 60 : 0));
@@ -560,7 +563,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (lane == 0 && (warp == 0 || warp == 13) && tq < 6) ZS_STAMP(71 + 4 * tq + (warp ? 60 : 0));
 #endif
                 if (i >= p.na &&
-                    !mbar_wait_sleep(&hd->a_empty[sa], (uint32_t)(((i >> p.lna) + 1) & 1), p.err, abort_flag))
+                    !mbar_wait_sleep(&hd->a_empty[sa], (uint32_t)((around + 1) & 1), p.err, abort_flag))
                     break;
 #ifdef ZS_TRACE
                 if (lane == 0 && (warp == 0 || warp == 13) && tq < 6) ZS_STAMP(72 + 4 * tq + (warp ? 60 : 0));
@@ -603,6 +606,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             kb += 3;
             while (kb >= R.gtk) { kb -= R.gtk; ++T; }
+            sa += 3;
+            while (sa >= p.na) { sa -= p.na; ++around; }
         }
         if (!*abort_flag)
             for (; sd < R.nseg; ++sd) drain(sd);
@@ -825,28 +830,39 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, int dev,
     // blocks of a GT row (so no TMA box crosses a row end) and leaves four
     // compressed slots (a slot is refilled while three feed the decoders);
     // failing that, two slots; failing that, a two-slot A ring.
+    // A ring of 4 slots (always fits: at most 2 x 32 KB of X + 64 KB of A +
+    // 2 x 12.3 KB of compressed data at the largest stream sizes). Compressed ring: the
+    // largest chunk of 4, 2 units that divides the K blocks of a GT row (so no
+    // TMA box crosses a row end) with four slots; else two slots; else
+    // single-unit chunks. (Measured at config 2: deeper A rings that force
+    // smaller chunks are slower -- the producers' TMA request rate binds.)
     p.nb = 2;
-    p.na = 4;
-    uint32_t fixed = (uint32_t)p.nb * p.b_slot + (uint32_t)p.na * kATileBytes;
     int cu = 1;
-    for (int want = 4; want >= 2 && cu == 1; want -= 2) {
-        for (int c = kMaxChunk; c > 1; c >>= 1) {
-            if (c > p.gtk || p.gtk % c) continue;
-            layout(c);
-            if (fixed + (uint32_t)want * p.c_slot <= budget) { cu = c; break; }
+    bool placed = false;
+    for (int na : {4}) {
+        p.na = na;
+        const uint32_t fixed = (uint32_t)p.nb * p.b_slot + (uint32_t)p.na * kATileBytes;
+        for (int want = 4; want >= 2 && !placed; want -= 2) {
+            for (int c = kMaxChunk; c >= 1 && !placed; c >>= 1) {
+                if (c > p.gtk || p.gtk % c) continue;
+                if (c == 1 && want == 4 && p.gtk % 2 == 0) continue;   // prefer 2 slots of 2 units
+                layout(c);
+                if (fixed + (uint32_t)want * p.c_slot <= budget) { cu = c; p.nc = want; placed = true; }
+            }
         }
+        if (placed) break;
     }
+    if (!placed) return cudaErrorInvalidValue;
     layout(cu);
-    if (fixed + 2 * p.c_slot > budget) {
-        p.na = 2;
-        fixed = (uint32_t)p.nb * p.b_slot + (uint32_t)p.na * kATileBytes;
-        if (fixed + 2 * p.c_slot > budget) return cudaErrorInvalidValue;
+#ifdef ZS_TRACE
+    if (const char* e = getenv("ZS_RINGS")) {   // "na,nc,cu" for experiments
+        int a = 0, b = 0, c = 0;
+        if (sscanf(e, "%d,%d,%d", &a, &b, &c) == 3) { p.na = a; p.nc = b; cu = c; layout(cu); }
     }
-    p.nc = (budget - fixed) / p.c_slot >= 4 ? 4 : 2;
+#endif
     auto ilog2 = [](int v) { int l = 0; while ((1 << l) < v) ++l; return l; };
     p.lcu = ilog2(p.cu);
     p.lnc = ilog2(p.nc);
-    p.lna = ilog2(p.na);
     p.lacc = ilog2(p.n_acc);
     p.off_b = base;
     p.off_a = p.off_b + (uint32_t)p.nb * p.b_slot;
