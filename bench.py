@@ -175,8 +175,35 @@ def run_reference(args):
         "wall_s": time.perf_counter() - t0}), flush=True)
 
 
+def run_ncu_attention(args):
+    """Profiling mode for decode attention: B=32, T=4096 (config 5), plain launches."""
+    import math
+
+    import torch
+
+    import zipserv_asplos26_b200 as zs
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    B, T, Hq, Hkv, D = 32, 4096, 32, 8, 128
+
+    def kv():
+        scale = torch.exp(torch.empty(Hkv, D, device=dev).uniform_(math.log(0.1), math.log(4.0), generator=gen))
+        return (torch.randn(B, T, Hkv, D, device=dev, generator=gen) * scale).to(torch.bfloat16)
+
+    kc, vc = zs.compress_kv(kv()), zs.compress_kv(kv())
+    q = torch.randn(B, Hq, D, device=dev, generator=gen).to(torch.bfloat16)
+    seq = torch.full((B,), T, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    for _ in range(args.warmup + args.steps):
+        zs.decode_attention(q, kc, vc, seq, Hkv, max_seqlen=T, out=out)
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_mode": True, "workload": "attention", "launches": args.warmup + args.steps}))
+
+
 def run_ncu(args):
     """Profiling mode: plain launches over the same rotating weights and X."""
+    if args.workload == "attention":
+        return run_ncu_attention(args)
     import torch
 
     import zipserv_asplos26_b200 as zs
@@ -432,7 +459,7 @@ def main():
                     choices=["config2", "llama8b", "attention", "roundtrip", "tp70b"],
                     help="config2 = the headline line; the others print one JSON line per case")
     args = ap.parse_args()
-    if args.workload != "config2" and args.impl == "ours":
+    if args.workload != "config2" and args.impl == "ours" and not args.ncu:
         return {"llama8b": run_llama8b, "attention": run_attention, "roundtrip": run_roundtrip,
                 "tp70b": run_tp70b}[args.workload](args)
     if args.impl == "reference":
