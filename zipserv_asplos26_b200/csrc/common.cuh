@@ -180,6 +180,33 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// CTA-scope release store / acquire load of a shared int.
+__device__ __forceinline__ void st_release_cta(int* a, int v) {
+    asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(a)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_cta(const int* a) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(a)) : "memory");
+    return v;
+}
+// Bounded wait until a shared counter reaches `want` (same error / abort contract as mbar_wait).
+__device__ __forceinline__ bool wait_tag_at_least(const int* tag, int want, unsigned* err, volatile int* abort_flag) {
+    if (ld_acquire_cta(tag) >= want) return true;
+    const long long t0 = clock64();
+    for (uint32_t it = 0;; ++it) {
+        __nanosleep(64);
+        if (ld_acquire_cta(tag) >= want) return true;
+        if ((it & 15) == 15) {
+            if (abort_flag && *abort_flag) return false;
+            if (clock64() - t0 > kWaitLimitCycles) {
+                if (err) atomicOr(err, kErrWaitTimeout);
+                if (abort_flag) *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

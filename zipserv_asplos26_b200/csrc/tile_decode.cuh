@@ -284,6 +284,72 @@ __device__ __forceinline__ void decode_mt_to_tile(const GtView& g, uint32_t lut_
     }
 }
 
+// Decode median tiles w0 and w0 + 1 of a staged GT (32 consecutive rows) into
+// the 128-byte-swizzled tile rows starting at `rows`, with the lane mapping of
+// decode_mt_to_tile. Both tiles' small-tile hf counts ride in one 16-bit-packed
+// scan (a median tile holds at most 1024 hf elements), so the per-tile prologue
+// (bitmap loads, scan, offsets) is shared and each lane has 8 independent rows
+// to interleave. Fallbacks of both tiles are patched in one loop.
+__device__ __forceinline__ void decode_mt2_to_tile(const GtView& g, uint32_t lut_lane, const DecodeTables& t, int w0,
+                                                   uint32_t rows) {
+    const int lane = threadIdx.x & 31;
+    const int s = lane & 15, rh = lane >> 4, kc = s >> 1, mr = s & 1;
+    uint32_t W1[2], W2[2], W3[2], IND[2], PLO[2], HC[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const uint32_t st = 16u * (uint32_t)(w0 + q) + (uint32_t)s;
+        const uint2 v1 = lds64(g.bm + 8u * st), v2 = lds64(g.bm + g.bstride + 8u * st),
+                    v3 = lds64(g.bm + 2u * g.bstride + 8u * st);
+        const uint32_t ilo = v1.x | v2.x | v3.x, ihi = v1.y | v2.y | v3.y;
+        PLO[q] = __popc(ilo);
+        HC[q] = PLO[q] + __popc(ihi);
+        IND[q] = rh ? ihi : ilo;
+        W1[q] = rh ? v1.y : v1.x;
+        W2[q] = rh ? v2.y : v2.x;
+        W3[q] = rh ? v3.y : v3.x;
+    }
+    const uint32_t hcp = HC[0] | (HC[1] << 16);
+    uint32_t x = hcp;
+#pragma unroll
+    for (int d = 1; d < 16; d <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, d, 16);
+        if (s >= d) x += y;
+    }
+    const uint32_t ex = x - hcp;
+    const uint2 mo0 = lds64(g.mt + 8u * (uint32_t)w0), mo1 = lds64(g.mt + 8u * (uint32_t)w0 + 8u);
+    uint32_t HS[2], FS[2];
+    HS[0] = mo0.x + (ex & 0xFFFFu) + (rh ? PLO[0] : 0u);
+    FS[0] = mo0.y + 64u * (uint32_t)s - (ex & 0xFFFFu) + (rh ? 32u - PLO[0] : 0u);
+    HS[1] = mo1.x + (ex >> 16) + (rh ? PLO[1] : 0u);
+    FS[1] = mo1.y + 64u * (uint32_t)s - (ex >> 16) + (rh ? 32u - PLO[1] : 0u);
+    const uint32_t sw = (uint32_t)kc ^ (4u * (uint32_t)rh);   // swizzled chunk of row r is sw ^ r
+    const uint32_t b0 = rows + 128u * (8u * (uint32_t)mr + 4u * (uint32_t)rh);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const uint32_t sel8 = 0x4440u | (uint32_t)r;
+            const uint32_t c1 = prmt(W1[q], 0, sel8), c2 = prmt(W2[q], 0, sel8), c3 = prmt(W3[q], 0, sel8);
+            const uint32_t pre = r ? (uint32_t)__popc(IND[q] & ((1u << (8 * r)) - 1u)) : 0u;
+            const uint32_t hf = min(HS[q] + pre, g.hf_cap);
+            uint32_t o[4];
+            decode_row_hf(c1, c2, c3, lut_lane, g.sm + hf, t, o);
+            sts128(b0 + 2048u * (uint32_t)q + 128u * (uint32_t)r + ((sw ^ (uint32_t)r) << 4), o[0], o[1], o[2], o[3]);
+        }
+    }
+    uint32_t fm0 = ~IND[0], fm1 = ~IND[1];
+    uint32_t f0 = FS[0], f1 = FS[1];
+    while (fm0 | fm1) {
+        const bool a = fm0 != 0;
+        const uint32_t fm = a ? fm0 : fm1;
+        const uint32_t j = __ffs(fm) - 1;
+        const uint32_t r = j >> 3, c = j & 7;
+        const uint32_t f = a ? f0 : f1;
+        sts16(b0 + (a ? 0u : 2048u) + 128u * r + ((sw ^ r) << 4) + 2u * c, lds16(g.full + 2u * min(f, g.full_cap)));
+        if (a) { fm0 &= fm0 - 1; ++f0; } else { fm1 &= fm1 - 1; ++f1; }
+    }
+}
+
 // Shared-memory footprint helpers for one staged GT.
 __host__ __device__ inline uint32_t round_up_u32(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 // Bytes reserved for a GT's hf stream: capacity plus 16 bytes of read slack

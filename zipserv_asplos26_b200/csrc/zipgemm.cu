@@ -50,13 +50,17 @@
 
 namespace zs {
 
-constexpr int kDecWarps = 24;
-constexpr int kCompWarp = 24;    // compressed producers: warps 24 and 27 (even / odd chunks)
-constexpr int kCompWarp1 = 27;
-constexpr int kBWarp = 25;
-constexpr int kMmaWarp = 26;
-constexpr int kGemmThreads = 28 * 32;
-constexpr int kTasksPerUnit = 8;
+// Decoder warps: each task is a pair of median tiles (32 rows x 64 columns), so
+// a unit (128 rows x 64 columns) is 4 tasks and the 16 decoders work on 4 units
+// at a time (one per A-ring slot).
+constexpr int kDecWarps = 16;
+constexpr int kTasksPerUnit = 4;
+constexpr int kUnitsInFlight = kDecWarps / kTasksPerUnit;
+constexpr int kCompWarp = 16;    // compressed producers: warps 16 and 19 (even / odd chunks)
+constexpr int kCompWarp1 = 19;
+constexpr int kBWarp = 17;
+constexpr int kMmaWarp = 18;
+constexpr int kGemmThreads = 20 * 32;
 constexpr int kMaxRing = 16;
 constexpr int kMaxAcc = 4;
 constexpr uint32_t kLutOffset = 1024;
@@ -125,10 +129,12 @@ struct GemmHeader {
     uint64_t acc_full[kMaxAcc], acc_empty[kMaxAcc];
     uint32_t tmem_base;
     int abort_flag;
+    int ctag[kMaxRing];   // newest chunk issued into each compressed slot (-1: none)
     int go[2];
     uint32_t drained[2];   // drain tasks finished, per partial-segment slot
     unsigned trace_gen;   // diagnostic builds only
 };
+static_assert(sizeof(GemmHeader) <= kLutOffset, "CTA header overlaps the spread table");
 
 #ifdef ZS_TRACE
 // Diagnostic build only (-DZS_TRACE): per-launch, per-CTA %globaltimer stamps.
@@ -281,6 +287,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&hd->acc_empty[s], 4 * (p.BN / 16));
         }
         hd->abort_flag = 0;
+        for (int s = 0; s < kMaxRing; ++s) hd->ctag[s] = -1;
         hd->drained[0] = hd->drained[1] = 0;
         fence_mbar_init();
     }
@@ -374,6 +381,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint64_t* bar = &hd->comp_full[s];
             if (lane == 0) {
                 if (i0 < 100) ZS_STAMP(110 + i0);
+                st_release_cta(&hd->ctag[s], cidx);   // slot s's previous fill has been consumed (and landed)
                 mbar_arrive_expect_tx(bar, total);
             }
             __syncwarp();
@@ -455,26 +463,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ZS_STAMP(1);
         }
     } else if (warp < kDecWarps) {
-        // Decoder warps. The task list is a sequence of rows of 24 tasks: a unit
-        // row holds the 8 median-tile tasks of 3 consecutive units, a drain row 24
-        // drain tasks of one segment (a segment needs ceil(4 * BN/16 / 24) rows).
-        // Warp w therefore always decodes median tile w % 8 of units w / 8 + 3j,
-        // and takes drain task 24 r + w of each drain row: no search per task.
+        // Decoder warps. The task list is a sequence of rows of 16 tasks: a unit
+        // row holds the 4 median-tile-pair tasks of 4 consecutive units, a drain
+        // row 16 drain tasks of one segment (a segment needs ceil(4 * BN/16 / 16)
+        // rows). Warp w therefore always decodes median-tile pair w % 4 of units
+        // w / 4 + 4j, and takes drain task 16 r + w of each drain row: no search
+        // per task.
         // Drains of all segments follow the last unit row, except when the CTA
         // has more segments than accumulators: then segment s is drained in the
         // unit row that starts after the first unit of segment s + 1.
         const DecodeTables tabs = make_decode_tables(p.start_exp);
         const uint32_t lut_lane = launder(smem_u32(lut)) + 4u * (uint32_t)lane;
         const int2* cinfo = reinterpret_cast<const int2*>(smem + kChunkInfo);
-        const int k = warp & 7, sub = k >> 2, w = k & 3;
+        const int k = warp & 3, sub = k >> 1, w = 2 * (k & 1);   // GT row, first median tile
         const int dsize = 4 * (p.BN / 16), drows = (dsize + kDecWarps - 1) / kDecWarps;
         const int cmask = p.cu - 1;
-        // mid-run drains: segment s before unit 3 * ceil((len0 + s * gtk + 1) / 3)
+        // mid-run drains: segment s before unit G * ceil((len0 + s * gtk + 1) / G), G = units in flight
+        constexpr int UG = kUnitsInFlight;
         int mid_end = 0;
         if (R.nseg > p.n_acc)
-            while (mid_end < R.nseg - 1 && 3 * ((R.len0 + mid_end * R.gtk + 3) / 3) < R.n) ++mid_end;
+            while (mid_end < R.nseg - 1 && UG * ((R.len0 + mid_end * R.gtk + UG) / UG) < R.n) ++mid_end;
         int sd = 0;
-        int dpos = 3 * ((R.len0 + 3) / 3);
+        int dpos = UG * ((R.len0 + UG) / UG);
         auto drain = [&](int s) {
             grid_dep_wait();   // C and the split-tile workspace may still be in use by the previous grid
             const int acc = s & (p.n_acc - 1);
@@ -531,18 +541,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
         };
-        // unit i = 3 g + warp / 8: its tile row T and K block kb advance by 3 units per row
-        int i = warp >> 3;
+        // unit i = UG g + warp / 4: its tile row T and K block kb advance by UG units per row
+        int i = warp >> 2;
         long long T = R.T0;
         int kb = R.off0 + i;
         while (kb >= R.gtk) { kb -= R.gtk; ++T; }
-        // A-ring slot and use count of unit i, advanced by 3 units per row (na is any size >= 2)
+        // A-ring slot and use count of unit i, advanced by UG units per row (na is any size >= 2)
         int sa = i % p.na, around = i / p.na;
-        for (int g = 0; 3 * g < R.n; ++g, i += 3) {
-            while (sd < mid_end && dpos == 3 * g) {
+        for (int g = 0; UG * g < R.n; ++g, i += UG) {
+            while (sd < mid_end && dpos == UG * g) {
                 drain(sd);
                 ++sd;
-                dpos = 3 * ((R.len0 + sd * R.gtk + 3) / 3);
+                dpos = UG * ((R.len0 + sd * R.gtk + UG) / UG);
             }
             if (*abort_flag) break;
             if (i < R.n) {
@@ -558,6 +568,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int tq = g;
                 if (lane == 0 && (warp == 0 || warp == 13) && tq < 6) ZS_STAMP(70 + 4 * tq + (warp ? 60 : 0));
 #endif
+                // A parity wait only separates neighbouring phases. A decoder can run up to
+                // ceil((UG - 1) / cu) + 1 chunks ahead of the oldest chunk in use, which may be
+                // two fills of one slot ahead; so it first waits until its chunk has been issued
+                // (the slot's previous fill has then landed and been consumed), after which the
+                // parity of the slot's barrier identifies the chunk exactly.
+                if (!wait_tag_at_least(&hd->ctag[cs], c, p.err, abort_flag)) break;
                 if (!mbar_wait_sleep(&hd->comp_full[cs], (uint32_t)((c >> p.lnc) & 1), p.err, abort_flag)) break;
 #ifdef ZS_TRACE
                 if (lane == 0 && (warp == 0 || warp == 13) && tq < 6) ZS_STAMP(71 + 4 * tq + (warp ? 60 : 0));
@@ -583,12 +599,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     gv.full_cap = p.full_area - f0;
                     const uint32_t rows =
                         smem0 + p.off_a + (uint32_t)sa * kATileBytes + 128u * (uint32_t)(64 * sub + 16 * w);
-                    ZS_GUARD(rows + 2048u <= smem0 + p.off_c && gv.sm + gv.hf_cap + 12u <= smem0 + p.smem_bytes &&
+                    ZS_GUARD(rows + 4096u <= smem0 + p.off_c && gv.sm + gv.hf_cap + 12u <= smem0 + p.smem_bytes &&
                                  gv.full + 2u * gv.full_cap + 2u <= smem0 + p.smem_bytes &&
                                  gv.bm + 2u * gv.bstride + 8u * 64u <= smem0 + p.smem_bytes &&
                                  gv.mt + 32u <= smem0 + p.smem_bytes,
                              0x400)
-                    decode_mt_to_tile(gv, lut_lane, tabs, w, rows);
+                    decode_mt2_to_tile(gv, lut_lane, tabs, w, rows);
                 }
 #ifdef ZS_TRACE
                 __syncwarp();
@@ -604,9 +620,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (k == 0 && i < 100) ZS_STAMP(10 + i);
                 }
             }
-            kb += 3;
+            kb += UG;
             while (kb >= R.gtk) { kb -= R.gtk; ++T; }
-            sa += 3;
+            sa += UG;
             while (sa >= p.na) { sa -= p.na; ++around; }
         }
         if (!*abort_flag)
