@@ -121,7 +121,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const AttnParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     AttnSmem& A = *reinterpret_cast<AttnSmem*>(smem);
-    uint32_t* lut = reinterpret_cast<uint32_t*>(smem + round_up_u32(sizeof(AttnSmem), 1024));
     const uint32_t smem0 = smem_u32(smem);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -134,7 +133,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
     const int G = p.G;
     const long long rb = ((long long)bh * p.T_pad) >> 6;   // first GT row of this (b, kv head)
 
-    fill_spread_table(lut, tid, kAttnThreads);
     for (int i = tid; i < kAttnMaxG * kAttnD; i += kAttnThreads) {
         const int h = i / kAttnD, d = i % kAttnD;
         A.qs[h][d] = h < G ? p.q[((size_t)b * p.Hq + hk * G + h) * kAttnD + d] : (uint16_t)0;
@@ -219,7 +217,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
     } else if (warp < kAttnDecWarps) {
         const int mat = warp >> 3, gc = (warp >> 2) & 1, mtile = warp & 3;
         const DecodeTables tabs = make_decode_tables(mat ? p.v.start_exp : p.k.start_exp);
-        const uint32_t lut_lane = launder(smem_u32(lut)) + 4u * (uint32_t)lane;
         int s = 0;
         uint32_t ph = 0;
         for (int pi = 0; pi < np; ++pi) {
@@ -239,7 +236,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             g.full_cap = p.full_cap / 2 - f0;
             const uint32_t rows = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes + 16384u * (uint32_t)mat +
                                   8192u * (uint32_t)gc + 2048u * (uint32_t)mtile;
-            decode_mt_to_tile(g, lut_lane, tabs, mtile, rows);
+            decode_mt_to_tile(g, tabs, mtile, rows);
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&A.tfull[s]);
@@ -478,7 +475,7 @@ cudaError_t launch_attention(cudaStream_t stream, const AttnCompressed& kc, cons
     p.full_cap = 2u * ffc;
     p.c_mat = round_up_u32(p.c_full + p.full_cap + 16u, 128);
     p.c_slot = 2u * p.c_mat;
-    p.off_tiles = round_up_u32(round_up_u32(sizeof(AttnSmem), 1024) + 4u * kLutWords, 1024);
+    p.off_tiles = round_up_u32(sizeof(AttnSmem), 1024);
     int dev = 0, max_smem = 232448;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);

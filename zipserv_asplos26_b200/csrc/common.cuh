@@ -207,6 +207,23 @@ __device__ __forceinline__ bool wait_tag_at_least(const int* tag, int want, unsi
     }
 }
 
+// Named CTA barriers (id 1..15; id 0 is __syncthreads). `count` counts threads
+// and must be a multiple of 32; arrive does not wait (release), sync waits
+// (acquire) for `count` arrivals in total.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// a / b for non-negative a, b: 32-bit division when a fits in 32 bits (the
+// common case; 64-bit division is a long instruction sequence).
+__host__ __device__ __forceinline__ long long div_nonneg(long long a, long long b) {
+    if (((unsigned long long)a >> 32) == 0 && ((unsigned long long)b >> 32) == 0)
+        return (long long)((unsigned)a / (unsigned)b);
+    return a / b;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -443,6 +460,43 @@ __device__ __forceinline__ void decode_row_hf(uint32_t c1, uint32_t c2, uint32_t
                                               uint32_t win, const DecodeTables& t, uint32_t (&o)[4]) {
     const uint32_t s1 = lds32(lut_lane + (c1 << 7)), s2 = lds32(lut_lane + (c2 << 7)),
                    s3 = lds32(lut_lane + (c3 << 7));
+    const uint32_t X = s1 + (s2 << 1) + (s3 << 2);        // code nibbles
+    const uint32_t sel = (s1 | s2 | s3) * 0x11111110u;    // hf-before-j nibbles
+    const uint32_t wa = win & ~3u;
+    const uint32_t sh = (win & 3u) * 8u;
+    const uint32_t q0 = lds32(wa), q1 = lds32(wa + 4), q2 = lds32(wa + 8);
+    const uint32_t lo = __funnelshift_r(q0, q1, sh);
+    const uint32_t hi = __funnelshift_r(q1, q2, sh);
+    const uint32_t s_lo = prmt(lo, hi, sel);
+    const uint32_t s_hi = prmt(lo, hi, sel >> 16);
+    const uint32_t hb_lo = lop_or_and(s_lo, 0x80808080u, prmt(t.thb0, t.thb1, X));
+    const uint32_t hb_hi = lop_or_and(s_hi, 0x80808080u, prmt(t.thb0, t.thb1, X >> 16));
+    const uint32_t lb_lo = lop_or_and(s_lo, 0x7F7F7F7Fu, prmt(t.tlb0, t.tlb1, X));
+    const uint32_t lb_hi = lop_or_and(s_hi, 0x7F7F7F7Fu, prmt(t.tlb0, t.tlb1, X >> 16));
+    o[0] = prmt(lb_lo, hb_lo, 0x5140);
+    o[1] = prmt(lb_lo, hb_lo, 0x7362);
+    o[2] = prmt(lb_hi, hb_hi, 0x5140);
+    o[3] = prmt(lb_hi, hb_hi, 0x7362);
+}
+
+// Table-free variant of decode_row_hf for callers that hold the three bitmap
+// words of a small tile's row half (w1, w2, w3: rows 4h .. 4h+3, one byte per
+// row) and decode row r (0..3) of them. The spread of a bitmap byte c (nibble
+// j = bit j) has byte k = {0x00, 0x01, 0x10, 0x11}[(c >> 2k) & 3], so one
+// byte permute of the constant 0x11100100 produces it from a selector whose
+// nibble k is bit group k of c; the selectors of bitmaps 1 and 2 are built
+// together in one word.
+__device__ __forceinline__ uint32_t bit_group_selectors(uint32_t x) {   // x: one byte in bytes 0 and/or 2
+    x = (x | (x << 4)) & 0x0F0F0F0Fu;
+    return (x | (x << 2)) & 0x33333333u;
+}
+__device__ __forceinline__ void decode_row_words(uint32_t w1, uint32_t w2, uint32_t w3, uint32_t r, uint32_t win,
+                                                 const DecodeTables& t, uint32_t (&o)[4]) {
+    constexpr uint32_t kSpreadBytes = 0x11100100u;
+    const uint32_t g12 = bit_group_selectors(prmt(w1, w2, r | ((4u + r) << 8)) & 0x00FF00FFu);
+    const uint32_t g3 = bit_group_selectors(prmt(w3, 0, 0x4440u | r));
+    const uint32_t s1 = prmt(kSpreadBytes, 0, g12), s2 = prmt(kSpreadBytes, 0, g12 >> 16),
+                   s3 = prmt(kSpreadBytes, 0, g3);
     const uint32_t X = s1 + (s2 << 1) + (s3 << 2);        // code nibbles
     const uint32_t sel = (s1 | s2 | s3) * 0x11111110u;    // hf-before-j nibbles
     const uint32_t wa = win & ~3u;

@@ -226,37 +226,49 @@ __device__ __forceinline__ void decode_gt_half_regs(const GtView& g, uint32_t lu
     }
 }
 
+// Inclusive scan of per-small-tile values over the 16 small tiles of a median
+// tile in ST order (s = 2 kc + mr), for the lane order of decode_mt_to_tile
+// (lane = 16 rh + 8 mr + kc; both row halves hold the same values). Values
+// may pack two 16-bit counts.
+__device__ __forceinline__ uint32_t st_order_inclusive_scan(uint32_t v, int lane) {
+    const int p = lane & 15;   // scan position = small tile p, held by lane 8 (p & 1) + (p >> 1)
+    uint32_t x = __shfl_sync(0xFFFFFFFFu, v, (lane & 16) | (8 * (p & 1) + (p >> 1)));
+#pragma unroll
+    for (int d = 1; d < 16; d <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, d, 16);
+        if (p >= d) x += y;
+    }
+    const int s = 2 * (lane & 7) + ((lane >> 3) & 1);   // this lane's small tile
+    return __shfl_sync(0xFFFFFFFFu, x, (lane & 16) | s);
+}
+
 // Decode median tile w (16 rows x 64 columns = 16 small tiles) of a staged GT
 // into 16 consecutive rows of a 128-byte-row bf16 tile in the UMMA canonical
 // 128-byte-swizzle layout (16-byte chunk c of tile row m at (c ^ (m & 7)) * 16).
 // `rows` is the tile address of the median tile's first row (a multiple of 8
 // rows into the tile).
 //
-// Lane L owns small tile s = L & 15 (column block kc = s / 2, row block
-// mr = s % 2) and rows 4 * (L >> 4) .. +3 of it. The hf offset of each small
-// tile is the median-tile base plus an exclusive scan of the small-tile hf
-// counts over the 16 lanes of the tile (ST order s = 2 kc + mr, csrc/L_API.cu
-// :623-644); the offset of a row adds the popcount of the indicator bits of
-// the rows above it. Each lane then decodes its rows with decode_row_hf and
-// finally overwrites its own fallback elements (code 0) in place, reading the
-// fallback stream in ST order.
-__device__ __forceinline__ void decode_mt_to_tile(const GtView& g, uint32_t lut_lane, const DecodeTables& t, int w,
-                                                  uint32_t rows) {
+// Lane L owns column block kc = L & 7 of row block mr = (L >> 3) & 1, i.e.
+// small tile s = 2 kc + mr, and rows 4 * (L >> 4) .. +3 of it. Lanes are
+// ordered (mr, kc) so that the 8 lanes of a quarter-warp store 8 different
+// 16-byte chunk positions of the swizzled tile (no bank conflicts). The hf
+// offset of each small tile is the median-tile base plus an exclusive scan of
+// the small-tile hf counts in ST order (s = 2 kc + mr, csrc/L_API.cu:623-644),
+// done by shuffling the counts into ST order, scanning and shuffling back; the
+// offset of a row adds the popcount of the indicator bits of the rows above
+// it. Each lane then decodes its rows with decode_row_hf and finally
+// overwrites its own fallback elements (code 0) in place, reading the fallback
+// stream in ST order.
+__device__ __forceinline__ void decode_mt_to_tile(const GtView& g, const DecodeTables& t, int w, uint32_t rows) {
     const int lane = threadIdx.x & 31;
-    const int s = lane & 15, rh = lane >> 4, kc = s >> 1, mr = s & 1;
+    const int rh = lane >> 4, kc = lane & 7, mr = (lane >> 3) & 1, s = 2 * kc + mr;
     const uint32_t st = 16u * (uint32_t)w + (uint32_t)s;
     const uint2 v1 = lds64(g.bm + 8u * st), v2 = lds64(g.bm + g.bstride + 8u * st),
                 v3 = lds64(g.bm + 2u * g.bstride + 8u * st);
     const uint32_t ilo = v1.x | v2.x | v3.x, ihi = v1.y | v2.y | v3.y;
     const uint32_t plo = __popc(ilo);
     const uint32_t hc = plo + __popc(ihi);
-    uint32_t x = hc;
-#pragma unroll
-    for (int d = 1; d < 16; d <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, d, 16);
-        if (s >= d) x += y;
-    }
-    const uint32_t excl = x - hc;
+    const uint32_t excl = st_order_inclusive_scan(hc, lane) - hc;
     const uint32_t hs = lds32(g.mt + 8u * (uint32_t)w) + excl + (rh ? plo : 0u);
     const uint32_t fs = lds32(g.mt + 8u * (uint32_t)w + 4u) + 64u * (uint32_t)s - excl + (rh ? 32u - plo : 0u);
     const uint32_t ind = rh ? ihi : ilo;   // indicator bits of this lane's 4 rows
@@ -265,12 +277,10 @@ __device__ __forceinline__ void decode_mt_to_tile(const GtView& g, uint32_t lut_
     const uint32_t sw = (uint32_t)kc ^ (4u * (uint32_t)rh);   // swizzled chunk of row r is sw ^ r
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-        const uint32_t sel8 = 0x4440u | (uint32_t)r;
-        const uint32_t c1 = prmt(w1, 0, sel8), c2 = prmt(w2, 0, sel8), c3 = prmt(w3, 0, sel8);
         const uint32_t pre = r ? (uint32_t)__popc(ind & ((1u << (8 * r)) - 1u)) : 0u;
         const uint32_t hf = min(hs + pre, g.hf_cap);
         uint32_t o[4];
-        decode_row_hf(c1, c2, c3, lut_lane, g.sm + hf, t, o);
+        decode_row_words(w1, w2, w3, (uint32_t)r, g.sm + hf, t, o);
         sts128(base + 128u * (uint32_t)r + ((sw ^ (uint32_t)r) << 4), o[0], o[1], o[2], o[3]);
     }
     uint32_t fm = ~ind;
@@ -290,10 +300,9 @@ __device__ __forceinline__ void decode_mt_to_tile(const GtView& g, uint32_t lut_
 // scan (a median tile holds at most 1024 hf elements), so the per-tile prologue
 // (bitmap loads, scan, offsets) is shared and each lane has 8 independent rows
 // to interleave. Fallbacks of both tiles are patched in one loop.
-__device__ __forceinline__ void decode_mt2_to_tile(const GtView& g, uint32_t lut_lane, const DecodeTables& t, int w0,
-                                                   uint32_t rows) {
+__device__ __forceinline__ void decode_mt2_to_tile(const GtView& g, const DecodeTables& t, int w0, uint32_t rows) {
     const int lane = threadIdx.x & 31;
-    const int s = lane & 15, rh = lane >> 4, kc = s >> 1, mr = s & 1;
+    const int rh = lane >> 4, kc = lane & 7, mr = (lane >> 3) & 1, s = 2 * kc + mr;
     uint32_t W1[2], W2[2], W3[2], IND[2], PLO[2], HC[2];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
@@ -309,13 +318,7 @@ __device__ __forceinline__ void decode_mt2_to_tile(const GtView& g, uint32_t lut
         W3[q] = rh ? v3.y : v3.x;
     }
     const uint32_t hcp = HC[0] | (HC[1] << 16);
-    uint32_t x = hcp;
-#pragma unroll
-    for (int d = 1; d < 16; d <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, d, 16);
-        if (s >= d) x += y;
-    }
-    const uint32_t ex = x - hcp;
+    const uint32_t ex = st_order_inclusive_scan(hcp, lane) - hcp;
     const uint2 mo0 = lds64(g.mt + 8u * (uint32_t)w0), mo1 = lds64(g.mt + 8u * (uint32_t)w0 + 8u);
     uint32_t HS[2], FS[2];
     HS[0] = mo0.x + (ex & 0xFFFFu) + (rh ? PLO[0] : 0u);
@@ -328,12 +331,10 @@ __device__ __forceinline__ void decode_mt2_to_tile(const GtView& g, uint32_t lut
     for (int q = 0; q < 2; ++q) {
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const uint32_t sel8 = 0x4440u | (uint32_t)r;
-            const uint32_t c1 = prmt(W1[q], 0, sel8), c2 = prmt(W2[q], 0, sel8), c3 = prmt(W3[q], 0, sel8);
             const uint32_t pre = r ? (uint32_t)__popc(IND[q] & ((1u << (8 * r)) - 1u)) : 0u;
             const uint32_t hf = min(HS[q] + pre, g.hf_cap);
             uint32_t o[4];
-            decode_row_hf(c1, c2, c3, lut_lane, g.sm + hf, t, o);
+            decode_row_words(W1[q], W2[q], W3[q], (uint32_t)r, g.sm + hf, t, o);
             sts128(b0 + 2048u * (uint32_t)q + 128u * (uint32_t)r + ((sw ^ (uint32_t)r) << 4), o[0], o[1], o[2], o[3]);
         }
     }

@@ -63,8 +63,8 @@ constexpr int kMmaWarp = 18;
 constexpr int kGemmThreads = 20 * 32;
 constexpr int kMaxRing = 16;
 constexpr int kMaxAcc = 4;
-constexpr uint32_t kLutOffset = 1024;
-constexpr uint32_t kOffsStage = kLutOffset + 4u * kLutWords;   // staged GT offsets: 64 units x 2 GT rows x int4
+constexpr uint32_t kHeaderBytes = 1024;
+constexpr uint32_t kOffsStage = kHeaderBytes;                    // staged GT offsets: 64 units x 2 GT rows x int4
 constexpr uint32_t kChunkInfo = kOffsStage + 2u * 2048u;         // [slot][unit][GT row] int2 offsets in a chunk
 constexpr int kMaxChunk = 4;
 constexpr uint32_t kStageEnd = kChunkInfo + (uint32_t)kMaxRing * kMaxChunk * 2 * 8;
@@ -134,7 +134,7 @@ struct GemmHeader {
     uint32_t drained[2];   // drain tasks finished, per partial-segment slot
     unsigned trace_gen;   // diagnostic builds only
 };
-static_assert(sizeof(GemmHeader) <= kLutOffset, "CTA header overlaps the spread table");
+static_assert(sizeof(GemmHeader) <= kHeaderBytes, "CTA header overlaps the offset staging area");
 
 #ifdef ZS_TRACE
 // Diagnostic build only (-DZS_TRACE): per-launch, per-CTA %globaltimer stamps.
@@ -159,10 +159,10 @@ __device__ unsigned long long* g_zs_trace = nullptr;
     } while (0)
 #endif
 
-__host__ __device__ __forceinline__ long long unit_begin(long long c, long long U, int G) { return c * U / G; }
+__host__ __device__ __forceinline__ long long unit_begin(long long c, long long U, int G) { return div_nonneg(c * U, G); }
 // CTA whose range holds unit g
 __host__ __device__ __forceinline__ long long unit_owner(long long g, long long U, int G) {
-    return ((g + 1) * G - 1) / U;
+    return div_nonneg((g + 1) * G - 1, U);
 }
 
 // Slot and phase of a ring of n mbarrier-guarded slots, advanced one use at a
@@ -230,7 +230,8 @@ struct UnitCursor {
 __device__ __forceinline__ void fetch_gt_offsets(const GemmParams& p, const CtaRange& R, int i, int4& e0, int4& e1) {
     e0 = e1 = make_int4(0, 0, 0, 0);
     if (i < R.n) {
-        const long long g = R.u0 + i, T = g / p.gtk, kb = g - T * p.gtk;
+        const int t = (R.off0 + i) / R.gtk, kb = R.off0 + i - t * R.gtk;   // tile offset and K block
+        const long long T = R.T0 + t;
         const long long gi = (2 * T) * p.gtk + kb;
         const int2* o = reinterpret_cast<const int2*>(p.gt_off);
         const int2 a0 = o[gi], a1 = o[gi + 1];
@@ -256,7 +257,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     }
 #endif
-    uint32_t* lut = reinterpret_cast<uint32_t*>(smem + kLutOffset);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x;
 
@@ -264,43 +264,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     R.gtk = p.gtk;
     R.u0 = unit_begin(blockIdx.x, p.units, G);
     R.n = (int)(unit_begin(blockIdx.x + 1, p.units, G) - R.u0);
-    R.T0 = R.u0 / p.gtk;
-    R.nseg = R.n > 0 ? (int)((R.u0 + R.n - 1) / p.gtk - R.T0 + 1) : 0;
+    R.T0 = div_nonneg(R.u0, p.gtk);
+    R.nseg = R.n > 0 ? (int)(div_nonneg(R.u0 + R.n - 1, p.gtk) - R.T0 + 1) : 0;
     R.off0 = (int)(R.u0 - R.T0 * p.gtk);
     R.len0 = min(p.gtk - R.off0, R.n);
 
-    // the producer's first GT-offset loads overlap the prologue
+    // The producers start fetching as soon as their own barriers exist: they
+    // initialise the compressed ring (one lane per slot), meet each other on
+    // named barrier 2 and only signal (bar.arrive) the CTA-wide start barrier 1,
+    // on which every other warp waits after its own set-up.
     int4 e0, e1;
     const bool producer = (warp == kCompWarp || warp == kCompWarp1);
     if (producer) fetch_gt_offsets(p, R, lane, e0, e1);
-    fill_spread_table(lut, tid, kGemmThreads);
-    if (tid == 0) {
-        if ((smem_u32(smem) & 1023u) && p.err) atomicOr(p.err, kErrStreamOverflow);
-        for (int s = 0; s < p.nc; ++s) {
-            mbar_init(&hd->comp_full[s], 1);
-            mbar_init(&hd->comp_empty[s], kTasksPerUnit * p.cu);
+    if (warp == kCompWarp) {
+        if (lane < p.nc) {
+            mbar_init(&hd->comp_full[lane], 1);
+            mbar_init(&hd->comp_empty[lane], kTasksPerUnit * p.cu);
         }
-        for (int s = 0; s < p.na; ++s) { mbar_init(&hd->a_full[s], kTasksPerUnit); mbar_init(&hd->a_empty[s], 1); }
-        for (int s = 0; s < p.nb; ++s) { mbar_init(&hd->b_full[s], 1); mbar_init(&hd->b_empty[s], 1); }
-        for (int s = 0; s < kMaxAcc; ++s) {
-            mbar_init(&hd->acc_full[s], 1);
-            mbar_init(&hd->acc_empty[s], 4 * (p.BN / 16));
-        }
-        hd->abort_flag = 0;
-        for (int s = 0; s < kMaxRing; ++s) hd->ctag[s] = -1;
-        hd->drained[0] = hd->drained[1] = 0;
+        if (lane < kMaxRing) hd->ctag[lane] = -1;
+        if (lane == 0) hd->abort_flag = 0;
         fence_mbar_init();
-    }
-    if (warp == kMmaWarp) {
+    } else if (warp == 0) {
+        if (lane < p.na) { mbar_init(&hd->a_full[lane], kTasksPerUnit); mbar_init(&hd->a_empty[lane], 1); }
+        if (lane < p.nb) { mbar_init(&hd->b_full[lane], 1); mbar_init(&hd->b_empty[lane], 1); }
+        if (lane < kMaxAcc) {
+            mbar_init(&hd->acc_full[lane], 1);
+            mbar_init(&hd->acc_empty[lane], 4 * (p.BN / 16));
+        }
+        if (lane < 2) hd->drained[lane] = 0;
+        if (lane == 0 && (smem_u32(smem) & 1023u) && p.err) atomicOr(p.err, kErrStreamOverflow);
+        fence_mbar_init();
+    } else if (warp == kMmaWarp) {
         tmem_alloc(&hd->tmem_base, kTmemCols);
         tmem_relinquish();
     }
     if (warp == kBWarp && lane == 0) prefetch_tmap(&maps.x);
     if (producer && lane < 4)
         prefetch_tmap(lane == 0 ? &maps.b1 : lane == 1 ? &maps.b2 : lane == 2 ? &maps.b3 : &maps.mt);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
+    if (producer) {
+        named_bar_sync(2, 64);
+        named_bar_arrive(1, kGemmThreads);
+    } else {
+        tc_fence_before();
+        named_bar_sync(1, kGemmThreads);
+        tc_fence_after();
+    }
 #ifdef ZS_TRACE
     const unsigned zs_gen = zs_trace_ptr ? hd->trace_gen : 0u;
 #endif
@@ -421,40 +429,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
+            // The issuing thread shares its scheduler with four decoder warps, so the
+            // per-unit path is kept short: shared-memory descriptors advance by
+            // constants (A slot: 16 KB = 1024 descriptor units; K step of 16
+            // elements: 32 bytes = 2 units) and the rings are plain counters.
             const uint32_t idesc = umma_idesc_bf16(128, p.BN);
-            Ring ra, rb, racc;
-            ra.init(p.na);
-            rb.init(p.nb);
+            const uint64_t da0 = umma_desc_sw128(smem0 + p.off_a), db0 = umma_desc_sw128(smem0 + p.off_b);
+            const uint32_t bstep = p.b_slot >> 4;
+            uint64_t da = da0, db = db0;
+            int sa = 0, sb = 0;
+            uint32_t pa = 0, pb = 0;
+            Ring racc;
             racc.init(p.n_acc);
+            uint32_t d = tmem_d;
             int seg_left = R.len0;
             bool first = true;
             for (int i = 0; i < R.n; ++i) {
                 if (first && racc.wrapped &&
                     !mbar_wait(&hd->acc_empty[racc.slot], racc.phase ^ 1u, p.err, abort_flag))
                     break;
-                if (!(p.debug & 4) && (!mbar_wait(&hd->a_full[ra.slot], ra.phase, p.err, abort_flag) ||
-                                        !mbar_wait(&hd->b_full[rb.slot], rb.phase, p.err, abort_flag)))
+                if (!mbar_wait(&hd->a_full[sa], pa, p.err, abort_flag) ||
+                    !mbar_wait(&hd->b_full[sb], pb, p.err, abort_flag))
                     break;
                 tc_fence_after();
-                const uint32_t a_addr = smem0 + p.off_a + (uint32_t)ra.slot * kATileBytes;
-                const uint32_t b_addr = smem0 + p.off_b + (uint32_t)rb.slot * p.b_slot;
-                const uint32_t d = tmem_d + (uint32_t)(racc.slot * p.BN);
-                ZS_GUARD(a_addr + kATileBytes <= smem0 + p.off_c && b_addr + p.b_slot <= smem0 + p.off_a &&
-                         racc.slot * p.BN + p.BN <= (int)kTmemCols, 0x10000)
-                if (!(p.debug & 8)) {
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        umma_bf16_ss(d, umma_desc_sw128(a_addr + 32 * k), umma_desc_sw128(b_addr + 32 * k), idesc,
-                                     (!first || k > 0) ? 1u : 0u);
+                ZS_GUARD(sa < p.na && sb < p.nb && racc.slot * p.BN + p.BN <= (int)kTmemCols, 0x10000) {
+                    umma_bf16_ss(d, da, db, idesc, first ? 0u : 1u);
+                    umma_bf16_ss(d, da + 2, db + 2, idesc, 1u);
+                    umma_bf16_ss(d, da + 4, db + 4, idesc, 1u);
+                    umma_bf16_ss(d, da + 6, db + 6, idesc, 1u);
                 }
-                umma_commit(&hd->a_empty[ra.slot]);
-                umma_commit(&hd->b_empty[rb.slot]);
-                ra.step();
-                rb.step();
+                umma_commit(&hd->a_empty[sa]);
+                umma_commit(&hd->b_empty[sb]);
+                if (++sa == p.na) { sa = 0; pa ^= 1u; da = da0; } else { da += 1024; }
+                if (++sb == p.nb) { sb = 0; pb ^= 1u; db = db0; } else { db += bstep; }
                 first = false;
                 if (--seg_left == 0) {
                     umma_commit(&hd->acc_full[racc.slot]);
                     racc.step();
+                    d = tmem_d + (uint32_t)(racc.slot * p.BN);
                     seg_left = min(p.gtk, R.n - i - 1);
                     first = true;
                 }
@@ -473,7 +485,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // has more segments than accumulators: then segment s is drained in the
         // unit row that starts after the first unit of segment s + 1.
         const DecodeTables tabs = make_decode_tables(p.start_exp);
-        const uint32_t lut_lane = launder(smem_u32(lut)) + 4u * (uint32_t)lane;
         const int2* cinfo = reinterpret_cast<const int2*>(smem + kChunkInfo);
         const int k = warp & 3, sub = k >> 1, w = 2 * (k & 1);   // GT row, first median tile
         const int dsize = 4 * (p.BN / 16), drows = (dsize + kDecWarps - 1) / kDecWarps;
@@ -604,7 +615,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                  gv.bm + 2u * gv.bstride + 8u * 64u <= smem0 + p.smem_bytes &&
                                  gv.mt + 32u <= smem0 + p.smem_bytes,
                              0x400)
-                    decode_mt2_to_tile(gv, lut_lane, tabs, w, rows);
+                    decode_mt2_to_tile(gv, tabs, w, rows);
                 }
 #ifdef ZS_TRACE
                 __syncwarp();
@@ -825,7 +836,7 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, int dev,
     p.units = mtiles * p.gtk;
     const int G = (int)std::min<long long>(di.sms, p.units);
 
-    // Shared memory: header | spread table | staging | B ring | A ring | compressed ring
+    // Shared memory: header | offset staging | B ring | A ring | compressed ring
     const uint32_t hfc = round_up_u32((uint32_t)max_hf, 16), ffc = round_up_u32((uint32_t)max_full, 8);
     p.b_slot = (uint32_t)p.BN * 128u;
     const uint32_t base = round_up_u32(kStageEnd, 1024);
@@ -841,39 +852,43 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, int dev,
         p.c_full[1] = p.c_full[0] + 2u * p.full_area + 16;
         p.c_slot = round_up_u32(p.c_full[1] + 2u * p.full_area + 16, 128);
     };
-    // Ring sizes are powers of two (slot and phase are shifts and masks on the
-    // decoders' paths). Chunk: the largest of 4, 2, 1 units that divides the K
-    // blocks of a GT row (so no TMA box crosses a row end) and leaves four
-    // compressed slots (a slot is refilled while three feed the decoders);
-    // failing that, two slots; failing that, a two-slot A ring.
-    // A ring of 4 slots (always fits: at most 2 x 32 KB of X + 64 KB of A +
-    // 2 x 12.3 KB of compressed data at the largest stream sizes). Compressed ring: the
-    // largest chunk of 4, 2 units that divides the K blocks of a GT row (so no
-    // TMA box crosses a row end) with four slots; else two slots; else
-    // single-unit chunks. (Measured at config 2: deeper A rings that force
-    // smaller chunks are slower -- the producers' TMA request rate binds.)
-    p.nb = 2;
+    // Compressed ring first: the largest chunk of 4, 2 units that divides the K
+    // blocks of a GT row (no TMA box crosses a row end) with four slots, else
+    // two slots, else single-unit chunks, next to the minimum A ring (one slot
+    // per unit the decoders work on) and a two-slot X ring. (Measured at config
+    // 2: rings that force smaller chunks are slower -- the producers' TMA
+    // request rate binds.) The rest deepens the A ring (the MMA may lag the
+    // decoders by a unit without stalling them) and the X ring (X tiles are
+    // L2 reads issued only when a slot frees).
     int cu = 1;
     bool placed = false;
-    for (int na : {4}) {
-        p.na = na;
-        const uint32_t fixed = (uint32_t)p.nb * p.b_slot + (uint32_t)p.na * kATileBytes;
-        for (int want = 4; want >= 2 && !placed; want -= 2) {
-            for (int c = kMaxChunk; c >= 1 && !placed; c >>= 1) {
-                if (c > p.gtk || p.gtk % c) continue;
-                if (c == 1 && want == 4 && p.gtk % 2 == 0) continue;   // prefer 2 slots of 2 units
-                layout(c);
-                if (fixed + (uint32_t)want * p.c_slot <= budget) { cu = c; p.nc = want; placed = true; }
-            }
+    const uint32_t min_fixed = 2u * p.b_slot + (uint32_t)kUnitsInFlight * kATileBytes;
+    for (int want = 4; want >= 2 && !placed; want -= 2) {
+        for (int c = kMaxChunk; c >= 1 && !placed; c >>= 1) {
+            if (c > p.gtk || p.gtk % c) continue;
+            if (c == 1 && want == 4 && p.gtk % 2 == 0) continue;   // prefer 2 slots of 2 units
+            layout(c);
+            if (min_fixed + (uint32_t)want * p.c_slot <= budget) { cu = c; p.nc = want; placed = true; }
         }
-        if (placed) break;
     }
     if (!placed) return cudaErrorInvalidValue;
     layout(cu);
+    p.na = kUnitsInFlight;
+    p.nb = 2;
+    {
+        const int pref[][2] = {{6, 3}, {5, 3}, {6, 2}, {5, 2}, {4, 3}};
+        for (const auto& q : pref) {
+            if ((uint32_t)q[1] * p.b_slot + (uint32_t)q[0] * kATileBytes + (uint32_t)p.nc * p.c_slot <= budget) {
+                p.na = q[0];
+                p.nb = q[1];
+                break;
+            }
+        }
+    }
 #ifdef ZS_TRACE
-    if (const char* e = getenv("ZS_RINGS")) {   // "na,nc,cu" for experiments
-        int a = 0, b = 0, c = 0;
-        if (sscanf(e, "%d,%d,%d", &a, &b, &c) == 3) { p.na = a; p.nc = b; cu = c; layout(cu); }
+    if (const char* e = getenv("ZS_RINGS")) {   // "na,nb,nc,cu" for experiments
+        int a = 0, b = 0, c = 0, d = 0;
+        if (sscanf(e, "%d,%d,%d,%d", &a, &b, &c, &d) == 4) { p.na = a; p.nb = b; p.nc = c; cu = d; layout(cu); }
     }
 #endif
     auto ilog2 = [](int v) { int l = 0; while ((1 << l) < v) ++l; return l; };
