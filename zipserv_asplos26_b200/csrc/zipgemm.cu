@@ -313,6 +313,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const unsigned zs_gen = zs_trace_ptr ? hd->trace_gen : 0u;
 #endif
     if (tid == 0) ZS_STAMP(0);
+    // The next grid on the stream may launch as soon as every CTA of this one
+    // is running: its CTAs then take SMs the moment this grid's CTAs exit,
+    // instead of idling until the slowest CTA of this grid reaches its
+    // epilogue. It waits for this grid (griddepcontrol.wait) before it reads
+    // X or touches C and the workspace.
+    if (tid == 0) grid_dep_launch();
     const uint32_t tmem_d = hd->tmem_base;
     volatile int* abort_flag = &hd->abort_flag;
     const uint32_t smem0 = smem_u32(smem);
@@ -649,8 +655,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // (concurrently) until every contributor of the respective tile has
     // published its partial tile; then the CTA sums its slice of the columns of
     // each such tile over the contributors in CTA order and writes bf16.
-    if (tid == 0) grid_dep_launch();   // the next grid may start on SMs this grid frees
-    grid_dep_wait();                   // C and the workspace may still be in use by the previous grid
+    grid_dep_wait();   // C and the workspace may still be in use by the previous grid
     const long long U = p.units;
     long long fT[2] = {-1, -1}, fcf[2] = {0, 0};
     int fn[2] = {0, 0}, fidx[2] = {0, 0}, fslot0[2] = {0, 0};
