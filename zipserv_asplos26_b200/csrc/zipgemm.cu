@@ -53,14 +53,18 @@ namespace zs {
 // Decoder warps: each task is a pair of median tiles (32 rows x 64 columns), so
 // a unit (128 rows x 64 columns) is 4 tasks and the 16 decoders work on 4 units
 // at a time (one per A-ring slot).
-constexpr int kDecWarps = 16;
+#ifndef ZS_DEC_WARPS
+#define ZS_DEC_WARPS 16
+#endif
+constexpr int kDecWarps = ZS_DEC_WARPS;
+static_assert(kDecWarps % 4 == 0, "decoder warps come in groups of four (one unit each)");
 constexpr int kTasksPerUnit = 4;
 constexpr int kUnitsInFlight = kDecWarps / kTasksPerUnit;
-constexpr int kCompWarp = 16;    // compressed producers: warps 16 and 19 (even / odd chunks)
-constexpr int kCompWarp1 = 19;
-constexpr int kBWarp = 17;
-constexpr int kMmaWarp = 18;
-constexpr int kGemmThreads = 20 * 32;
+constexpr int kCompWarp = kDecWarps;   // compressed producers: warps kDecWarps and kDecWarps + 3 (even / odd chunks)
+constexpr int kCompWarp1 = kDecWarps + 3;
+constexpr int kBWarp = kDecWarps + 1;
+constexpr int kMmaWarp = kDecWarps + 2;
+constexpr int kGemmThreads = (kDecWarps + 4) * 32;
 constexpr int kMaxRing = 16;
 constexpr int kMaxAcc = 4;
 constexpr uint32_t kHeaderBytes = 1024;
@@ -566,6 +570,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // A-ring slot and use count of unit i, advanced by UG units per row (na is any size >= 2)
         int sa = i % p.na, around = i / p.na;
         for (int g = 0; UG * g < R.n; ++g, i += UG) {
+#ifdef ZS_TRACE
+            if (lane == 0 && warp == 0 && g < 6) ZS_STAMP(131 + 4 * g);
+#endif
             while (sd < mid_end && dpos == UG * g) {
                 drain(sd);
                 ++sd;
@@ -583,7 +590,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int cs = c & (p.nc - 1);
 #ifdef ZS_TRACE
                 const int tq = g;
-                if (lane == 0 && (warp == 0 || warp == 13) && tq < 6) ZS_STAMP(70 + 4 * tq + (warp ? 60 : 0));
+                if (lane == 0 && warp == 0 && tq < 6) ZS_STAMP(70 + 4 * tq );
 #endif
                 // A parity wait only separates neighbouring phases. A decoder can run up to
                 // ceil((UG - 1) / cu) + 1 chunks ahead of the oldest chunk in use, which may be
@@ -593,13 +600,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (!wait_tag_at_least(&hd->ctag[cs], c, p.err, abort_flag)) break;
                 if (!mbar_wait_sleep(&hd->comp_full[cs], (uint32_t)((c >> p.lnc) & 1), p.err, abort_flag)) break;
 #ifdef ZS_TRACE
-                if (lane == 0 && (warp == 0 || warp == 13) && tq < 6) ZS_STAMP(71 + 4 * tq + (warp ? 60 : 0));
+                if (lane == 0 && warp == 0 && tq < 6) ZS_STAMP(71 + 4 * tq );
 #endif
                 if (i >= p.na &&
                     !mbar_wait_sleep(&hd->a_empty[sa], (uint32_t)((around + 1) & 1), p.err, abort_flag))
                     break;
 #ifdef ZS_TRACE
-                if (lane == 0 && (warp == 0 || warp == 13) && tq < 6) ZS_STAMP(72 + 4 * tq + (warp ? 60 : 0));
+                if (lane == 0 && warp == 0 && tq < 6) ZS_STAMP(72 + 4 * tq );
 #endif
                 if (2 * T + sub < p.mgt && !(p.debug & 1)) {
                     const uint32_t base = launder(smem0 + p.off_c + (uint32_t)cs * p.c_slot);
@@ -625,9 +632,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
 #ifdef ZS_TRACE
                 __syncwarp();
-                if (lane == 0 && (warp == 0 || warp == 13) && tq < 6) ZS_STAMP(73 + 4 * tq + (warp ? 60 : 0));
+                if (lane == 0 && warp == 0 && tq < 6) ZS_STAMP(73 + 4 * tq );
 #endif
                 fence_proxy_async_smem();   // the tensor core reads the tile through the async proxy
+#ifdef ZS_TRACE
+                if (lane == 0 && warp == 0 && tq < 6) ZS_STAMP(130 + 4 * tq);
+#endif
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&hd->a_full[sa]);
@@ -881,7 +891,8 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, int dev,
     p.na = kUnitsInFlight;
     p.nb = 2;
     {
-        const int pref[][2] = {{6, 3}, {5, 3}, {6, 2}, {5, 2}, {4, 3}};
+        constexpr int U = kUnitsInFlight;
+        const int pref[][2] = {{U + 2, 3}, {U + 1, 3}, {U + 2, 2}, {U + 1, 2}, {U, 3}};
         for (const auto& q : pref) {
             if ((uint32_t)q[1] * p.b_slot + (uint32_t)q[0] * kATileBytes + (uint32_t)p.nc * p.c_slot <= budget) {
                 p.na = q[0];
