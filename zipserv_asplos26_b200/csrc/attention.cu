@@ -10,14 +10,11 @@
 // so one 64-token page of one (b, kv head) is one GT row (two GTs).
 //
 // Grid: (B * Hkv) x S splits; each CTA owns a contiguous range of pages of one
-// (b, kv head) and the G = Hq / Hkv query heads that share it:
-//   warp 8      producer: bulk-copies chunks of consecutive pages (K and V
-//               streams are contiguous in GT order, one copy per stream)
-//   warps 0..3  decode K (lane = token, 64 dims each) and form the fp32 dot
-//               products with the G query heads
-//   warps 4..7  decode V into a shared bf16 tile
-//   then an online base-2 softmax (warp h = query head h) and an fp32 P.V
-//   accumulation (thread = pair of dims x token quarter).
+// (b, kv head) and the G = Hq / Hkv query heads that share it. Warp roles are
+// listed at attn_decode_kernel: one producer warp bulk-copies the compressed
+// pages, 16 decoder warps expand K and V pages into 128-byte-swizzled bf16
+// tiles with the small-tile decoder shared with ZipGEMM, and two math warps
+// take alternate pages (S = Q K^T, online base-2 softmax, O += P V).
 // With S > 1 every CTA writes (m, l, unnormalised O) to a caller-provided fp32
 // workspace and combine_kernel merges the splits; with S = 1 the CTA writes
 // the normalised bf16 output itself.

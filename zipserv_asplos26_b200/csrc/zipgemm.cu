@@ -20,21 +20,23 @@
 // order, so results are deterministic). The grid never exceeds one CTA per SM,
 // so the CTAs of a grid are co-resident and the end-of-kernel wait on the other
 // contributors is safe. Consecutive GEMMs overlap through programmatic
-// dependent launch (only X, C and the workspace wait for the previous grid).
+// dependent launch: every CTA allows the next grid to launch right after its
+// set-up, and only X, C and the workspace wait for the previous grid.
 //
-// Inside a CTA (896 threads):
-//   warps 24, 27 compressed producers (alternate chunks): per unit, 1-D bulk copies of both GTs'
-//                bitmaps, median offsets, sign/mantissa and fallback streams
-//                into a ring of shared-memory slots
-//   warp 25      X producer: 2-D TMA (128-byte swizzle) of the 64 x BN tile
-//   warp 26      MMA issuer: tcgen05.mma kind::f16, M=128, N=BN, K=16 x 4 per
+// Inside a CTA (kDecWarps + 4 warps; 640 threads with the default 16 decoders):
+//   warps D, D+3 compressed producers (D = kDecWarps; alternate chunks of 1, 2
+//                or 4 units): 2-D TMA loads of the bitmaps and median offsets
+//                of both GT rows, 1-D bulk copies of their sign/mantissa and
+//                fallback streams, into a ring of shared-memory slots
+//   warp D+1     X producer: 2-D TMA (128-byte swizzle) of the 64 x BN tile
+//   warp D+2     MMA issuer: tcgen05.mma kind::f16, M=128, N=BN, K=16 x 4 per
 //                unit, operands from shared memory, fp32 accumulators in TMEM
 //                (up to four, one per segment in flight)
-//   warps 0-23   decoders. A unit is eight tasks, one per median tile (16 rows
-//                x 64 columns); task t of the CTA's task list goes to warp
-//                t % 24. The decoded tile lands in the A ring in the UMMA
-//                canonical K-major 128-byte-swizzle layout. "Drain" tasks (4
-//                per segment, one per TMEM lane quarter) move a finished
+//   warps 0..D-1 decoders. A unit is four tasks, one per pair of median tiles
+//                (32 rows x 64 columns); warp w decodes pair w % 4 of units
+//                w / 4 + (D / 4) j. The decoded tile lands in the A ring in the
+//                UMMA canonical K-major 128-byte-swizzle layout. "Drain" tasks
+//                (16 columns of one TMEM lane quarter each) move a finished
 //                accumulator to C or to the workspace.
 #include <cudaTypedefs.h>
 
