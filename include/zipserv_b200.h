@@ -116,6 +116,36 @@ int zs_decode_attention_noalloc(void* stream, const uint16_t* d_q, const void* c
                                 int Hkv, int D, int T_pad, int max_seqlen, float softmax_scale, int num_splits,
                                 uint16_t* d_out, int* splits_used, unsigned* d_err);
 
+/* ---- On-disk TCA-TBE container (file format version 1) -------------------
+ * No counterpart in the reference, which keeps no serialised compressed form
+ * (its benchmarks re-encode the dense checkpoint at start-up,
+ * kernel_benchmark/bench_zipserv_gemm_sweep.cu:290-345). The file holds the
+ * arrays the encoders produce (csrc/L_API.cu:559-771 layout) with a CRC-32 per
+ * array; all buffers here are HOST memory. Errors: 301 (cudaErrorFileNotFound)
+ * when the file cannot be opened, 999 (cudaErrorUnknown) on a short read or
+ * write, 1 (cudaErrorInvalidValue) for bad arguments, a foreign or damaged
+ * file (magic, version, sizes, checksum). */
+typedef struct ZsTcatbeInfo {
+    int64_t rows, cols;
+    int32_t start_exp, max_hf, max_full;
+    int32_t top[7];
+    int64_t total_hf, total_full;   /* valid lengths of the two streams */
+    int32_t has_st_counts;          /* 1 when the small-tile counts are stored */
+} ZsTcatbeInfo;
+
+/* Write one compressed matrix. Array lengths follow from info: sm total_hf
+ * bytes, full total_full elements, bitmaps rows*cols/64 words each, st_counts
+ * 2*#ST ints (only when info->has_st_counts), mt_off 2*#MT, gt_off 2*(#GT+1). */
+int zs_tcatbe_save(const char* path, const ZsTcatbeInfo* info, const uint8_t* sm, const uint16_t* full,
+                   const uint64_t* b1, const uint64_t* b2, const uint64_t* b3, const int* st_counts,
+                   const int* mt_off, const int* gt_off);
+/* Read the header (sizes and scalars) so the caller can size its buffers. */
+int zs_tcatbe_read_info(const char* path, ZsTcatbeInfo* info);
+/* Read every array into caller buffers sized from zs_tcatbe_read_info and
+ * verify the checksums; st_counts may be NULL to skip them. */
+int zs_tcatbe_load(const char* path, ZsTcatbeInfo* info, uint8_t* sm, uint16_t* full, uint64_t* b1,
+                   uint64_t* b2, uint64_t* b3, int* st_counts, int* mt_off, int* gt_off);
+
 #ifdef __cplusplus
 }
 #endif

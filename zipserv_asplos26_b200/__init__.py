@@ -9,3 +9,4 @@ __all__ = ["Compressed", "analyze_exponents", "compress", "compress_host", "deco
 from .attention import compress_kv, decode_attention, flash_attn_with_kvcache, pad_kv_by_kv_head  # noqa: E402,F401
 
 __all__ += ["compress_kv", "decode_attention", "flash_attn_with_kvcache", "pad_kv_by_kv_head"]
+from . import store  # noqa: E402,F401  (save / load of compressed matrices)
