@@ -116,6 +116,48 @@ int zs_decode_attention_noalloc(void* stream, const uint16_t* d_q, const void* c
                                 int Hkv, int D, int T_pad, int max_seqlen, float softmax_scale, int num_splits,
                                 uint16_t* d_out, int* splits_used, unsigned* d_err);
 
+/* ---- Paged compressed KV cache with online page append --------------------
+ * The reference compresses a whole KV cache at once in its head-major layout
+ * (kernel_benchmark/bench_zipserv_decode_attention.py:347-354) and, for online
+ * compression, re-runs the matrix encoder pipeline
+ * (bench_kv_cache_zipserv_compress_token_scaling.cu:1606-1647). Here a pool
+ * holds fixed-window compressed pages of 64 tokens x 128 dims of one KV head
+ * (two GTs each) at physical page slots P = block * Hkv + head; the streams of
+ * each page are appended to shared stream pools at positions taken from a
+ * device cursor, and page_off records them. All pointers are device memory. */
+typedef struct ZsKvPool {
+    uint8_t* d_sm;                 /* sign/mantissa stream pool, hf_capacity bytes, 16-byte aligned */
+    uint16_t* d_full;              /* fallback stream pool, full_capacity elements, 16-byte aligned */
+    uint64_t* d_b1, *d_b2, *d_b3;  /* [num_pages * 2 * 64] bitmaps */
+    int* d_mt_off;                 /* [num_pages * 2 * 8] median-tile offsets */
+    int* d_page_off;               /* [num_pages * 6]: {hf, fallback} starts of GT 0, GT 1 and the end */
+    unsigned long long* d_cursor;  /* [2]: next free hf byte, next free fallback element (start at 0) */
+    int64_t hf_capacity, full_capacity;
+    int num_pages;                 /* num_blocks * Hkv */
+    int start_exp;                 /* (top[0] - 1) mod 256 of the window below */
+    const int* d_top7;             /* the pool's fixed exponent window */
+} ZsKvPool;
+
+/* Compress whole pages of new tokens into the pool. d_x is token-major
+ * [B][64 * npg][Hkv][D] bf16 (D = 128); page (b, j, h) goes to physical page
+ * d_dst_pages[(b * npg + j) * Hkv + h] (negative: skipped). Encoding is
+ * byte-identical to zs_encode of the 64 x 128 page with the pool's window.
+ * A page that does not fit in the stream pools sets bit 2 in *d_err. */
+int zs_kv_append_pages(void* stream, const ZsKvPool* pool, const uint16_t* d_x, int B, int npg, int Hkv, int D,
+                       const int* d_dst_pages, unsigned* d_err);
+
+/* Decode attention over paged compressed K/V (same outputs and workspace rules
+ * as zs_decode_attention). Logical page g of sequence b is block
+ * d_block_table[b * max_blocks + g]; d_seqlens[b] is the sequence length. When
+ * d_tail_k / d_tail_v ([B][64][Hkv][D] bf16) are given, a sequence whose length
+ * is not a multiple of 64 ends with a dense page read from them (its first
+ * len % 64 tokens); otherwise every page must be in the pools. */
+int zs_decode_attention_paged(void* stream, const uint16_t* d_q, const ZsKvPool* k, const ZsKvPool* v,
+                              const int* d_block_table, int max_blocks, const int* d_seqlens, const uint16_t* d_tail_k,
+                              const uint16_t* d_tail_v, int B, int Hq, int Hkv, int D, int max_seqlen,
+                              float softmax_scale, int num_splits, float* d_ws, size_t ws_bytes, uint16_t* d_out,
+                              int* splits_used, unsigned* d_err);
+
 /* ---- On-disk TCA-TBE container (file format version 1) -------------------
  * No counterpart in the reference, which keeps no serialised compressed form
  * (its benchmarks re-encode the dense checkpoint at start-up,

@@ -29,6 +29,9 @@
 
 namespace zs {
 
+#ifndef ZS_ATTN_P_SPLIT
+#define ZS_ATTN_P_SPLIT 1   // P.V with P as bf16 high part + bf16 residual (0: high part only, as FlashAttention)
+#endif
 constexpr int kAttnMaxG = 8;        // query heads per KV head
 constexpr int kAttnD = 128;         // head dim (two 64-wide GTs)
 constexpr int kAttnDecWarps = 16;   // one median-tile task of K or V per page each
@@ -48,6 +51,7 @@ struct AttnStream {
     const uint64_t* b3;
     const int* mt_off;
     const int* gt_off;
+    const int* page_off;   // paged layout: [pages][6] stream offsets (GT 0 start, GT 1 start, end)
     int max_hf, max_full, start_exp;
 };
 
@@ -65,6 +69,14 @@ struct AttnParams {
     uint32_t off_tiles, off_slots;
     int nslots;               // depth of the page rings (compressed slots and decoded tiles): 3, or 2 for large streams
     unsigned* err;
+    // Paged layout (block_table != nullptr): logical page g of sequence b is
+    // physical page block_table[b * max_blocks + g] * Hkv + kv head; when the
+    // dense tails are given, a sequence whose length is not a multiple of 64
+    // ends with a dense page read from tail_k / tail_v ([B][64][Hkv][D] bf16).
+    const int* block_table;
+    int max_blocks, num_blocks;
+    const uint16_t* tail_k;
+    const uint16_t* tail_v;
 };
 
 struct AttnSmem {
@@ -123,8 +135,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh = blockIdx.x, split = blockIdx.y;
     const int b = bh / p.Hkv, hk = bh % p.Hkv;
-    const int len = max(0, min(p.seqlens[b], p.T_pad));
+    const int len = p.block_table ? max(0, min(p.seqlens[b], 64 * p.max_blocks)) : max(0, min(p.seqlens[b], p.T_pad));
     const int npages = (len + 63) >> 6;
+    const bool has_tail = p.tail_k != nullptr && (len & 63) != 0;
+    // the last page of a paged sequence with a dense tail is read from tail_k / tail_v
+    auto is_dense_page = [&](int g) { return has_tail && g == npages - 1; };
     const int pg0 = split * p.pages_per_split;
     const int np = max(0, min(npages, pg0 + p.pages_per_split) - pg0);
     const int G = p.G;
@@ -153,29 +168,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
         const int mat = lane / 6, kind = lane % 6;
         const AttnStream& S = mat ? p.v : p.k;
         const AttnStream& So = lane < 3 ? p.k : p.v;
+        // page record: the lane's GT offset entry and the page's first GT index
+        struct PageRec { int2 e; long long gt0; };
         auto fetch = [&](int pi) {
-            int2 e = make_int2(0, 0);
-            if (pi < np && lane < 6) e = reinterpret_cast<const int2*>(So.gt_off)[(rb + pg0 + pi) * 2 + (lane % 3)];
-            return e;
+            PageRec r{make_int2(0, 0), (rb + pg0 + pi) * 2};
+            if (pi >= np) return r;
+            if (p.block_table) {
+                const int g = pg0 + pi;
+                if (is_dense_page(g)) return r;
+                int blk = p.block_table[(size_t)b * p.max_blocks + g];
+                if (blk < 0 || blk >= p.num_blocks) {
+                    if (lane == 0 && p.err) atomicOr(p.err, kErrStreamOverflow);
+                    blk = 0;
+                }
+                const long long P = (long long)blk * p.Hkv + hk;
+                r.gt0 = 2 * P;
+                if (lane < 6) r.e = reinterpret_cast<const int2*>(So.page_off)[P * 3 + (lane % 3)];
+            } else if (lane < 6) {
+                r.e = reinterpret_cast<const int2*>(So.gt_off)[(rb + pg0 + pi) * 2 + (lane % 3)];
+            }
+            return r;
         };
-        int2 cur = fetch(0);
+        PageRec cur = fetch(0);
         int s = 0;
         uint32_t ph = 0;
         bool ok = true;
         for (int pi = 0; pi < np && ok; ++pi) {
-            const int2 nxt = fetch(pi + 1);   // in flight while this page is issued
+            const PageRec nxt = fetch(pi + 1);   // in flight while this page is issued
             if (lane == 0 && pi >= p.nslots) ok = mbar_wait(&A.cempty[s], ph ^ 1u, p.err, abort_flag);
             ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             const int mb = 3 * mat;
-            const int h0 = __shfl_sync(0xFFFFFFFFu, cur.x, mb), f0 = __shfl_sync(0xFFFFFFFFu, cur.y, mb);
-            const int h1 = __shfl_sync(0xFFFFFFFFu, cur.x, mb + 1), f1 = __shfl_sync(0xFFFFFFFFu, cur.y, mb + 1);
-            const int h2 = __shfl_sync(0xFFFFFFFFu, cur.x, mb + 2), f2 = __shfl_sync(0xFFFFFFFFu, cur.y, mb + 2);
+            const int h0 = __shfl_sync(0xFFFFFFFFu, cur.e.x, mb), f0 = __shfl_sync(0xFFFFFFFFu, cur.e.y, mb);
+            const int h1 = __shfl_sync(0xFFFFFFFFu, cur.e.x, mb + 1), f1 = __shfl_sync(0xFFFFFFFFu, cur.e.y, mb + 1);
+            const int h2 = __shfl_sync(0xFFFFFFFFu, cur.e.x, mb + 2), f2 = __shfl_sync(0xFFFFFFFFu, cur.e.y, mb + 2);
             uint8_t* slot = smem + p.off_slots + (size_t)s * p.c_slot + (size_t)mat * p.c_mat;
-            const long long gt0 = (rb + pg0 + pi) * 2;
+            const long long gt0 = cur.gt0;
             uint32_t size = 0, dst = 0;
             const void* src = nullptr;
-            if (lane < 12) {
+            if (lane < 12 && !is_dense_page(pg0 + pi)) {   // a dense tail page is read by the decoders
                 if (kind < 3) {
                     size = 1024u;
                     dst = 1024u * (uint32_t)kind;
@@ -233,7 +264,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             g.full_cap = p.full_cap / 2 - f0;
             const uint32_t rows = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes + 16384u * (uint32_t)mat +
                                   8192u * (uint32_t)gc + 2048u * (uint32_t)mtile;
-            decode_mt_to_tile(g, tabs, mtile, rows);
+            if (is_dense_page(pg0 + pi)) {
+                // dense tail page: rows 16 mtile .. +15 (tokens), columns 64 gc .. +63 of
+                // K or V, zero past the sequence end, in the swizzled tile layout
+                const uint16_t* tb = (mat ? p.tail_v : p.tail_k) + ((size_t)b * 64 * p.Hkv + hk) * kAttnD + 64 * gc;
+                const int tl = len & 63;
+#pragma unroll
+                for (int c = lane; c < 128; c += 32) {
+                    const int rr = c >> 3, ch = c & 7, m = 16 * mtile + rr;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    if (m < tl) v = *reinterpret_cast<const uint4*>(tb + (size_t)m * p.Hkv * kAttnD + 8 * ch);
+                    sts128(rows + 128u * (uint32_t)rr + (((uint32_t)ch ^ ((uint32_t)rr & 7u)) << 4), v.x, v.y, v.z,
+                           v.w);
+                }
+            } else {
+                decode_mt_to_tile(g, tabs, mtile, rows);
+            }
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&A.tfull[s]);
@@ -334,8 +380,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
                     ldsm_x4_t(addr, b0, b1, b2, b3);
                     mma_rows8(o[2 * np2][0], o[2 * np2][1], pa0[kk], pa2[kk], b0, b1);
                     mma_rows8(o[2 * np2 + 1][0], o[2 * np2 + 1][1], pa0[kk], pa2[kk], b2, b3);
+#if ZS_ATTN_P_SPLIT
                     mma_rows8(o[2 * np2][0], o[2 * np2][1], pl0[kk], pl2[kk], b0, b1);
                     mma_rows8(o[2 * np2 + 1][0], o[2 * np2 + 1][1], pl0[kk], pl2[kk], b2, b3);
+#endif
                 }
             }
             __syncwarp();
@@ -425,19 +473,28 @@ static int attn_default_splits(int B, int Hkv, int max_pages) {
     return std::min(s, std::max(1, max_pages));
 }
 
-cudaError_t launch_attention(cudaStream_t stream, const AttnCompressed& kc, const AttnCompressed& vc,
-                             const uint16_t* q, const int* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D,
-                             int T_pad, int max_seqlen, float softmax_scale, int num_splits, float* ws,
-                             size_t ws_bytes, unsigned* err, int* splits_used) {
-    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D != kAttnD || T_pad <= 0 || T_pad % 64)
-        return cudaErrorInvalidValue;
+static cudaError_t attention_core(cudaStream_t stream, const AttnCompressed& kc, const AttnCompressed& vc,
+                                  const uint16_t* q, const int* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D,
+                                  int T_pad, int max_seqlen, float softmax_scale, int num_splits, float* ws,
+                                  size_t ws_bytes, unsigned* err, int* splits_used, const AttnPaged* pg) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D != kAttnD) return cudaErrorInvalidValue;
+    if (!pg && (T_pad <= 0 || T_pad % 64)) return cudaErrorInvalidValue;
     const int G = Hq / Hkv;
     if (G > kAttnMaxG) return cudaErrorInvalidValue;
-    if (!q || !seqlens || !out || max_seqlen < 0 || max_seqlen > T_pad) return cudaErrorInvalidValue;
+    if (!q || !seqlens || !out || max_seqlen < 0) return cudaErrorInvalidValue;
+    if (!pg && max_seqlen > T_pad) return cudaErrorInvalidValue;
+    if (pg) {
+        if (!pg->block_table || pg->max_blocks <= 0 || pg->num_blocks <= 0 || !pg->k_page_off || !pg->v_page_off ||
+            max_seqlen > 64 * pg->max_blocks || (reinterpret_cast<uintptr_t>(pg->k_page_off) & 7u) ||
+            (reinterpret_cast<uintptr_t>(pg->v_page_off) & 7u))
+            return cudaErrorInvalidValue;
+        if ((pg->tail_k == nullptr) != (pg->tail_v == nullptr) || !aligned16(pg->tail_k) || !aligned16(pg->tail_v))
+            return cudaErrorInvalidValue;
+    }
     const AttnCompressed* cs[2] = {&kc, &vc};
     for (const AttnCompressed* c : cs) {
-        if (!c->b1 || !c->b2 || !c->b3 || !c->mt_off || !c->gt_off) return cudaErrorInvalidValue;
-        if (c->rows != B * Hkv * T_pad || c->cols != D) return cudaErrorInvalidValue;
+        if (!c->b1 || !c->b2 || !c->b3 || !c->mt_off || (!pg && !c->gt_off)) return cudaErrorInvalidValue;
+        if (!pg && (c->rows != B * Hkv * T_pad || c->cols != D)) return cudaErrorInvalidValue;
         if (c->max_hf < 0 || c->max_full < 0 || c->max_hf > 4096 + 15 || c->max_full > 4096 + 7)
             return cudaErrorInvalidValue;
         if (!aligned16(c->sm) || !aligned16(c->full) || !aligned16(c->b1) || !aligned16(c->b2) ||
@@ -458,6 +515,15 @@ cudaError_t launch_attention(cudaStream_t stream, const AttnCompressed& kc, cons
     };
     fill(p.k, kc);
     fill(p.v, vc);
+    if (pg) {
+        p.k.page_off = pg->k_page_off;
+        p.v.page_off = pg->v_page_off;
+        p.block_table = pg->block_table;
+        p.max_blocks = pg->max_blocks;
+        p.num_blocks = pg->num_blocks;
+        p.tail_k = pg->tail_k;
+        p.tail_v = pg->tail_v;
+    }
     p.q = q; p.seqlens = seqlens; p.out = out; p.ws = ws; p.err = err;
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.T_pad = T_pad; p.S = S;
     p.pages_per_split = (max_pages + S - 1) / S;
@@ -531,6 +597,22 @@ static cudaError_t noalloc_ws_ptr(float** out) {
     }
     *out = ptrs[dev];
     return cudaSuccess;
+}
+
+cudaError_t launch_attention(cudaStream_t stream, const AttnCompressed& kc, const AttnCompressed& vc,
+                             const uint16_t* q, const int* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D,
+                             int T_pad, int max_seqlen, float softmax_scale, int num_splits, float* ws,
+                             size_t ws_bytes, unsigned* err, int* splits_used) {
+    return attention_core(stream, kc, vc, q, seqlens, out, B, Hq, Hkv, D, T_pad, max_seqlen, softmax_scale,
+                          num_splits, ws, ws_bytes, err, splits_used, nullptr);
+}
+
+cudaError_t launch_attention_paged(cudaStream_t stream, const AttnCompressed& kc, const AttnCompressed& vc,
+                                   const AttnPaged& pg, const uint16_t* q, const int* seqlens, uint16_t* out, int B,
+                                   int Hq, int Hkv, int D, int max_seqlen, float softmax_scale, int num_splits,
+                                   float* ws, size_t ws_bytes, unsigned* err, int* splits_used) {
+    return attention_core(stream, kc, vc, q, seqlens, out, B, Hq, Hkv, D, 64, max_seqlen, softmax_scale,
+                          num_splits, ws, ws_bytes, err, splits_used, &pg);
 }
 
 size_t attn_noalloc_ws_bytes() { return kNoAllocWsFloats * sizeof(float); }

@@ -127,6 +127,51 @@ extern "C" int zs_decode_attention_noalloc(void* stream, const uint16_t* d_q, co
                                         max_seqlen, softmax_scale, num_splits, d_err, splits_used);
 }
 
+extern "C" int zs_kv_append_pages(void* stream, const ZsKvPool* pool, const uint16_t* d_x, int B, int npg, int Hkv,
+                                  int D, const int* d_dst_pages, unsigned* d_err) {
+    if (!pool) return cudaErrorInvalidValue;
+    return zs::launch_kv_append((cudaStream_t)stream, d_x, B, npg, Hkv, D, d_dst_pages, pool->num_pages,
+                                pool->d_top7, pool->d_sm, pool->d_full, pool->d_b1, pool->d_b2, pool->d_b3,
+                                pool->d_mt_off, pool->d_page_off, pool->d_cursor, pool->hf_capacity,
+                                pool->full_capacity, d_err);
+}
+
+static zs::AttnCompressed pool_view(const ZsKvPool& p) {
+    zs::AttnCompressed c{};
+    c.sm = p.d_sm;
+    c.full = p.d_full;
+    c.b1 = p.d_b1;
+    c.b2 = p.d_b2;
+    c.b3 = p.d_b3;
+    c.mt_off = p.d_mt_off;
+    c.gt_off = nullptr;
+    c.rows = 0;
+    c.cols = 128;
+    c.max_hf = 4096;     // a page GT of the pool may hold up to 4096 hf bytes
+    c.max_full = 4096;   // and up to 4096 fallback elements
+    c.start_exp = p.start_exp;
+    return c;
+}
+
+extern "C" int zs_decode_attention_paged(void* stream, const uint16_t* d_q, const ZsKvPool* k, const ZsKvPool* v,
+                                         const int* d_block_table, int max_blocks, const int* d_seqlens,
+                                         const uint16_t* d_tail_k, const uint16_t* d_tail_v, int B, int Hq, int Hkv,
+                                         int D, int max_seqlen, float softmax_scale, int num_splits, float* d_ws,
+                                         size_t ws_bytes, uint16_t* d_out, int* splits_used, unsigned* d_err) {
+    if (!k || !v || Hkv <= 0 || k->num_pages != v->num_pages || k->num_pages % Hkv) return cudaErrorInvalidValue;
+    zs::AttnPaged pg{};
+    pg.block_table = d_block_table;
+    pg.max_blocks = max_blocks;
+    pg.num_blocks = k->num_pages / Hkv;
+    pg.k_page_off = k->d_page_off;
+    pg.v_page_off = v->d_page_off;
+    pg.tail_k = d_tail_k;
+    pg.tail_v = d_tail_v;
+    return zs::launch_attention_paged((cudaStream_t)stream, pool_view(*k), pool_view(*v), pg, d_q, d_seqlens, d_out,
+                                      B, Hq, Hkv, D, max_seqlen, softmax_scale, num_splits, d_ws, ws_bytes, d_err,
+                                      splits_used);
+}
+
 // ---------------------- reference GPU ABI (C++ names) -----------------------
 cudaError_t BF16TripleBitmap_MM_API(cudaStream_t stream, const uint8_t* SignMantissa,
                                     const __nv_bfloat16* CompressedFull, const uint64_t* Bitmap1,

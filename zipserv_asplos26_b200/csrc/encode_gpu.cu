@@ -262,29 +262,31 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* gt_hf_cnt
     }
 }
 
-__global__ void __launch_bounds__(128) encode_kernel(const uint16_t* __restrict__ in, int K, const int* top,
-                                                      const int* __restrict__ gt_off, uint8_t* __restrict__ sm,
-                                                      uint16_t* __restrict__ full, uint64_t* __restrict__ b1,
-                                                      uint64_t* __restrict__ b2, uint64_t* __restrict__ b3,
-                                                      int* __restrict__ st_counts, int* __restrict__ mt_off) {
-    __shared__ uint8_t lut[256];
-    __shared__ __align__(16) uint8_t bmp[3][512];      // bitmap bytes: [plane][st*8 + r]
-    __shared__ int cnt[513];                            // per row-task hf counts, stream order
-    __shared__ int wsum[4];
-    __shared__ __align__(16) uint8_t sbuf[4096 + 16];   // compacted hf bytes
-    __shared__ __align__(16) uint16_t fbuf[4096 + 8];   // compacted fallbacks
-    build_code_lut(lut, top);
-    const int gtk = K >> 6;
-    const long long gt = blockIdx.x;
-    const long long r0 = (gt / gtk) * 64, c0 = (gt % gtk) * 64;
-    const int t = threadIdx.x, m = t & 63, kc0 = 4 * (t >> 6);
+// Shared-memory state of one GT being encoded by a group of 128 threads.
+struct GtEncodeSmem {
+    __align__(16) uint8_t bmp[3][512];   // bitmap bytes: [plane][st*8 + r]
+    int cnt[513];                        // per row-task exclusive hf prefix, stream order; [512] = total
+    int wsum[4];
+    __align__(16) uint8_t sbuf[4096 + 16];    // compacted hf bytes (zero padded to 16)
+    __align__(16) uint16_t fbuf[4096 + 8];    // compacted fallbacks (zero padded to 8)
+};
+
+// Encode one 64x64 GT whose element (m, c) is at src[m * ld + c] into `S`
+// (bitmaps, prefix counts, compacted streams), with the 128 threads t of one
+// group synchronising on named barrier `bar` (a 128-thread CTA passes 0).
+// Row-task mapping: thread t owns row m = t & 63 and column blocks
+// kc = 4*(t>>6) .. +3; each row-task is 8 elements (16 bytes). Returns the
+// unpadded hf count (the fallback count is 4096 minus it).
+__device__ int encode_gt_core(const uint16_t* __restrict__ src, long long ld, const uint8_t* lut, GtEncodeSmem& S,
+                              int t, int bar) {
+    const int m = t & 63, kc0 = 4 * (t >> 6);
     const int w = m >> 4, mr = (m >> 3) & 1, r = m & 7;
     uint4 rows[4];
     uint32_t codes[4];  // per row-task: 8 codes as nibbles
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int kc = kc0 + i;
-        rows[i] = *reinterpret_cast<const uint4*>(in + (r0 + m) * K + c0 + kc * 8);
+        rows[i] = *reinterpret_cast<const uint4*>(src + (long long)m * ld + kc * 8);
         const uint32_t wv[4] = {rows[i].x, rows[i].y, rows[i].z, rows[i].w};
         uint32_t p1 = 0, p2 = 0, p3 = 0, nib = 0;
 #pragma unroll
@@ -298,78 +300,185 @@ __global__ void __launch_bounds__(128) encode_kernel(const uint16_t* __restrict_
         }
         codes[i] = nib;
         const int st = w * 16 + 2 * kc + mr;
-        bmp[0][st * 8 + r] = (uint8_t)p1;
-        bmp[1][st * 8 + r] = (uint8_t)p2;
-        bmp[2][st * 8 + r] = (uint8_t)p3;
-        cnt[st * 8 + r] = __popc(p1 | p2 | p3);
+        S.bmp[0][st * 8 + r] = (uint8_t)p1;
+        S.bmp[1][st * 8 + r] = (uint8_t)p2;
+        S.bmp[2][st * 8 + r] = (uint8_t)p3;
+        S.cnt[st * 8 + r] = __popc(p1 | p2 | p3);
     }
-    __syncthreads();
+    named_bar_sync(bar, 128);
     // exclusive scan of cnt[0..511] (thread t owns entries 4t..4t+3)
-    int v0 = cnt[4 * t], v1 = cnt[4 * t + 1], v2 = cnt[4 * t + 2], v3 = cnt[4 * t + 3];
+    int v0 = S.cnt[4 * t], v1 = S.cnt[4 * t + 1], v2 = S.cnt[4 * t + 2], v3 = S.cnt[4 * t + 3];
     int s = v0 + v1 + v2 + v3, inc = s;
     for (int o = 1; o < 32; o <<= 1) {
         const int a = __shfl_up_sync(0xFFFFFFFFu, inc, o);
         if ((t & 31) >= o) inc += a;
     }
-    if ((t & 31) == 31) wsum[t >> 5] = inc;
-    __syncthreads();
+    if ((t & 31) == 31) S.wsum[t >> 5] = inc;
+    named_bar_sync(bar, 128);
     int wbase = 0;
-    for (int i = 0; i < (t >> 5); ++i) wbase += wsum[i];
-    const int total_hf = wsum[0] + wsum[1] + wsum[2] + wsum[3];
-    __syncthreads();
+    for (int i = 0; i < (t >> 5); ++i) wbase += S.wsum[i];
+    const int total_hf = S.wsum[0] + S.wsum[1] + S.wsum[2] + S.wsum[3];
+    named_bar_sync(bar, 128);
     int e = wbase + inc - s;
-    cnt[4 * t] = e; e += v0;
-    cnt[4 * t + 1] = e; e += v1;
-    cnt[4 * t + 2] = e; e += v2;
-    cnt[4 * t + 3] = e;
-    if (t == 0) cnt[512] = total_hf;
-    __syncthreads();
+    S.cnt[4 * t] = e; e += v0;
+    S.cnt[4 * t + 1] = e; e += v1;
+    S.cnt[4 * t + 2] = e; e += v2;
+    S.cnt[4 * t + 3] = e;
+    if (t == 0) S.cnt[512] = total_hf;
+    named_bar_sync(bar, 128);
     // scatter into the compaction buffers
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int kc = kc0 + i;
         const int idx = (w * 16 + 2 * kc + mr) * 8 + r;
-        int hp = cnt[idx];
+        int hp = S.cnt[idx];
         int fp = idx * 8 - hp;
         const uint32_t wv[4] = {rows[i].x, rows[i].y, rows[i].z, rows[i].w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const uint32_t v = (wv[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
             if ((codes[i] >> (4 * j)) & 7u) {
-                sbuf[hp++] = (uint8_t)(((v >> 8) & 0x80u) | (v & 0x7Fu));
+                S.sbuf[hp++] = (uint8_t)(((v >> 8) & 0x80u) | (v & 0x7Fu));
             } else {
-                fbuf[fp++] = (uint16_t)v;
+                S.fbuf[fp++] = (uint16_t)v;
             }
         }
     }
     const int total_full = 4096 - total_hf;
     const int pad_hf = (total_hf + 15) & ~15, pad_full = (total_full + 7) & ~7;
-    if (t < pad_hf - total_hf) sbuf[total_hf + t] = 0;
-    if (t < pad_full - total_full) fbuf[total_full + t] = 0;
-    // per-ST counts and median offsets
+    if (t < pad_hf - total_hf) S.sbuf[total_hf + t] = 0;
+    if (t < pad_full - total_full) S.fbuf[total_full + t] = 0;
+    named_bar_sync(bar, 128);
+    return total_hf;
+}
+
+// Write the encoded GT's bitmaps (GT slot g of the bitmap arrays), median
+// offsets, optional small-tile counts, and both padded streams at (h0, f0).
+__device__ void write_gt(const GtEncodeSmem& S, int t, long long g, int total_hf, uint8_t* __restrict__ sm,
+                         uint16_t* __restrict__ full, long long h0, long long f0, uint64_t* __restrict__ b1,
+                         uint64_t* __restrict__ b2, uint64_t* __restrict__ b3, int* __restrict__ st_counts,
+                         int* __restrict__ mt_off) {
     if (t < 64) {
-        const int a = cnt[t * 8], b = cnt[t * 8 + 8];
-        st_counts[2 * (gt * 64 + t)] = b - a;
-        st_counts[2 * (gt * 64 + t) + 1] = 64 - (b - a);
+        if (st_counts) {
+            const int a = S.cnt[t * 8], b = S.cnt[t * 8 + 8];
+            st_counts[2 * (g * 64 + t)] = b - a;
+            st_counts[2 * (g * 64 + t) + 1] = 64 - (b - a);
+        }
     } else if (t < 68) {
         const int q = t - 64;
-        mt_off[2 * (gt * 4 + q)] = cnt[q * 128];
-        mt_off[2 * (gt * 4 + q) + 1] = q * 1024 - cnt[q * 128];
+        mt_off[2 * (g * 4 + q)] = S.cnt[q * 128];
+        mt_off[2 * (g * 4 + q) + 1] = q * 1024 - S.cnt[q * 128];
+    }
+    {
+        const int plane = t >> 6, st = t & 63;  // threads 0..127 cover planes 0, 1; plane 2 below
+        const uint64_t* bsrc = reinterpret_cast<const uint64_t*>(&S.bmp[0][0]);
+        uint64_t* dst = plane == 0 ? b1 : b2;
+        dst[g * 64 + st] = bsrc[plane * 64 + st];
+        if (t < 64) b3[g * 64 + t] = bsrc[128 + t];
+    }
+    const int pad_hf = (total_hf + 15) & ~15, pad_full = (4096 - total_hf + 7) & ~7;
+    for (int i = t; i < pad_hf / 16; i += 128)
+        *reinterpret_cast<uint4*>(sm + h0 + 16 * i) = reinterpret_cast<const uint4*>(S.sbuf)[i];
+    for (int i = t; i < pad_full / 8; i += 128)
+        *reinterpret_cast<uint4*>(full + f0 + 8 * i) = reinterpret_cast<const uint4*>(S.fbuf)[i];
+}
+
+__global__ void __launch_bounds__(128) encode_kernel(const uint16_t* __restrict__ in, int K, const int* top,
+                                                      const int* __restrict__ gt_off, uint8_t* __restrict__ sm,
+                                                      uint16_t* __restrict__ full, uint64_t* __restrict__ b1,
+                                                      uint64_t* __restrict__ b2, uint64_t* __restrict__ b3,
+                                                      int* __restrict__ st_counts, int* __restrict__ mt_off) {
+    __shared__ uint8_t lut[256];
+    __shared__ GtEncodeSmem S;
+    build_code_lut(lut, top);
+    const int gtk = K >> 6;
+    const long long gt = blockIdx.x;
+    const long long r0 = (gt / gtk) * 64, c0 = (gt % gtk) * 64;
+    const int t = threadIdx.x;
+    const int total_hf = encode_gt_core(in + r0 * K + c0, K, lut, S, t, 0);
+    write_gt(S, t, gt, total_hf, sm, full, gt_off[2 * gt], gt_off[2 * gt + 1], b1, b2, b3, st_counts, mt_off);
+}
+
+// Online KV page append (no counterpart kernel in the reference, whose KV
+// benchmarks compress a whole cache at once with the matrix encoder,
+// kernel_benchmark/bench_kv_cache_zipserv_compress_token_scaling.cu:1606-1647).
+// One CTA per page of 64 tokens x 128 dims of one KV head: x holds B sequences
+// of npg pages each, token-major [B][64 npg][Hkv][128]; page (b, j, h) is
+// encoded with the pool's fixed exponent window into physical page
+// P = dst_pages[(b * npg + j) * Hkv + h] (negative: skipped). Its two GTs go to
+// bitmap / median-offset slots 2P and 2P+1; its streams are appended to the
+// pools at positions taken from the pool cursors (one atomic per stream and
+// page, so the two GTs' streams are contiguous) and recorded in
+// page_off[6P .. 6P+5] = {hf, fallback} starts of GT 0 and GT 1, and the end.
+// A page that does not fit in the pools sets kErrStreamOverflow and records
+// an empty page.
+__global__ void __launch_bounds__(256) kv_append_kernel(const uint16_t* __restrict__ x, int Hkv,
+                                                         const int* __restrict__ dst_pages, int num_pages,
+                                                         const int* top, uint8_t* __restrict__ sm,
+                                                         uint16_t* __restrict__ full, uint64_t* __restrict__ b1,
+                                                         uint64_t* __restrict__ b2, uint64_t* __restrict__ b3,
+                                                         int* __restrict__ mt_off, int* __restrict__ page_off,
+                                                         unsigned long long* cursor, long long hf_cap,
+                                                         long long full_cap, unsigned* err) {
+    __shared__ uint8_t lut[256];
+    __shared__ GtEncodeSmem S[2];
+    __shared__ long long base[2];
+    const long long i = blockIdx.x;
+    const int P = dst_pages[i];
+    if (P < 0) return;
+    if (P >= num_pages) {
+        if (threadIdx.x == 0 && err) atomicOr(err, kErrStreamOverflow);
+        return;
+    }
+    build_code_lut(lut, top);
+    constexpr long long D = 128;
+    const long long h = i % Hkv, bj = i / Hkv;   // bj = b * npg + j
+    const uint16_t* src = x + (bj * 64 * Hkv + h) * D;
+    const int t = threadIdx.x & 127, g = threadIdx.x >> 7;
+    const int hf = encode_gt_core(src + 64 * g, (long long)Hkv * D, lut, S[g], t, 1 + g);
+    __syncthreads();
+    const int hf0 = S[0].cnt[512], hf1 = S[1].cnt[512];
+    const long long ph0 = (hf0 + 15) & ~15, ph1 = (hf1 + 15) & ~15;
+    const long long pf0 = (4096 - hf0 + 7) & ~7, pf1 = (4096 - hf1 + 7) & ~7;
+    if (threadIdx.x == 0) {
+        const long long hb = (long long)atomicAdd(&cursor[0], (unsigned long long)(ph0 + ph1));
+        const long long fb = (long long)atomicAdd(&cursor[1], (unsigned long long)(pf0 + pf1));
+        const bool ok = hb + ph0 + ph1 <= hf_cap && fb + pf0 + pf1 <= full_cap && hb + ph0 + ph1 <= 0x7FFFFFFFll &&
+                        fb + pf0 + pf1 <= 0x7FFFFFFFll;
+        int* po = page_off + 6LL * P;
+        if (ok) {
+            base[0] = hb;
+            base[1] = fb;
+            po[0] = (int)hb; po[1] = (int)fb;
+            po[2] = (int)(hb + ph0); po[3] = (int)(fb + pf0);
+            po[4] = (int)(hb + ph0 + ph1); po[5] = (int)(fb + pf0 + pf1);
+        } else {
+            base[0] = -1;
+            for (int k = 0; k < 6; ++k) po[k] = 0;
+            if (err) atomicOr(err, kErrStreamOverflow);
+        }
     }
     __syncthreads();
-    // bitmaps: 64 x u64 per plane
-    {
-        const int plane = t >> 6, st = t & 63;  // threads 0..127 cover planes 0,1; plane 2 below
-        const uint64_t* src = reinterpret_cast<const uint64_t*>(&bmp[0][0]);
-        uint64_t* dst = plane == 0 ? b1 : b2;
-        dst[gt * 64 + st] = src[plane * 64 + st];
-        if (t < 64) b3[gt * 64 + t] = src[128 + t];
-    }
-    const long long h0 = gt_off[2 * gt], f0 = gt_off[2 * gt + 1];
-    for (int i = t; i < pad_hf / 16; i += 128)
-        *reinterpret_cast<uint4*>(sm + h0 + 16 * i) = reinterpret_cast<const uint4*>(sbuf)[i];
-    for (int i = t; i < pad_full / 8; i += 128)
-        *reinterpret_cast<uint4*>(full + f0 + 8 * i) = reinterpret_cast<const uint4*>(fbuf)[i];
+    if (base[0] < 0) return;
+    write_gt(S[g], t, 2LL * P + g, hf, sm, full, base[0] + (g ? ph0 : 0), base[1] + (g ? pf0 : 0), b1, b2, b3,
+             nullptr, mt_off);
+}
+
+cudaError_t launch_kv_append(cudaStream_t s, const uint16_t* x, int B, int npg, int Hkv, int D,
+                             const int* dst_pages, int num_pages, const int* d_top, uint8_t* sm, uint16_t* full,
+                             uint64_t* b1, uint64_t* b2, uint64_t* b3, int* mt_off, int* page_off,
+                             unsigned long long* cursor, long long hf_cap, long long full_cap, unsigned* err) {
+    if (B < 0 || npg < 0 || Hkv <= 0 || D != 128 || num_pages <= 0) return cudaErrorInvalidValue;
+    const long long n = (long long)B * npg * Hkv;
+    if (n == 0) return cudaSuccess;
+    if (n > 0x7FFFFFFFll) return cudaErrorInvalidValue;
+    if (!x || !dst_pages || !d_top || !sm || !full || !b1 || !b2 || !b3 || !mt_off || !page_off || !cursor)
+        return cudaErrorInvalidValue;
+    if (!aligned16(x) || !aligned16(sm) || !aligned16(full) || hf_cap < 0 || full_cap < 0)
+        return cudaErrorInvalidValue;
+    kv_append_kernel<<<(unsigned)n, 256, 0, s>>>(x, Hkv, dst_pages, num_pages, d_top, sm, full, b1, b2, b3, mt_off,
+                                                 page_off, cursor, hf_cap, full_cap, err);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_encode(cudaStream_t s, const uint16_t* in, int M, int K, const int* d_top, uint8_t* sm,

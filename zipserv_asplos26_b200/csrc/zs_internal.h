@@ -24,6 +24,12 @@ cudaError_t launch_encode(cudaStream_t s, const uint16_t* in, int M, int K, cons
                           int* mt_off, int* gt_off, int* gt_hf_cnt, int* gt_full_cnt, int* hf_prefix,
                           int* full_prefix, int* d_max_hf, int* d_max_full, int* d_total_hf, int* d_total_full);
 
+// Online KV page append into a page pool (see kv_append_kernel).
+cudaError_t launch_kv_append(cudaStream_t s, const uint16_t* x, int B, int npg, int Hkv, int D,
+                             const int* dst_pages, int num_pages, const int* d_top, uint8_t* sm, uint16_t* full,
+                             uint64_t* b1, uint64_t* b2, uint64_t* b3, int* mt_off, int* page_off,
+                             unsigned long long* cursor, long long hf_cap, long long full_cap, unsigned* err);
+
 cudaError_t launch_decompress(cudaStream_t s, const uint8_t* sm, const uint16_t* full, const uint64_t* b1,
                               const uint64_t* b2, const uint64_t* b3, const int* mt_off, const int* gt_off,
                               int max_hf, int max_full, int start_exp, uint16_t* out, int M, int K,
@@ -52,6 +58,26 @@ cudaError_t launch_attention(cudaStream_t s, const AttnCompressed& k, const Attn
                              const int* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int T_pad,
                              int max_seqlen, float softmax_scale, int num_splits, float* ws, size_t ws_bytes,
                              unsigned* err, int* splits_used);
+
+// Paged compressed KV (see attn_decode_kernel): physical page of logical page g
+// of sequence b and KV head h is block_table[b * max_blocks + g] * Hkv + h;
+// page_off holds per physical page {hf, fallback} starts of its two GTs and
+// the end. tail_k / tail_v (nullable, [B][64][Hkv][D] bf16) hold each
+// sequence's last, not yet compressed, page when its length is not a
+// multiple of 64.
+struct AttnPaged {
+    const int* block_table;
+    int max_blocks, num_blocks;
+    const int* k_page_off;
+    const int* v_page_off;
+    const uint16_t* tail_k;
+    const uint16_t* tail_v;
+};
+
+cudaError_t launch_attention_paged(cudaStream_t s, const AttnCompressed& k, const AttnCompressed& v,
+                                   const AttnPaged& pg, const uint16_t* q, const int* seqlens, uint16_t* out, int B,
+                                   int Hq, int Hkv, int D, int max_seqlen, float softmax_scale, int num_splits,
+                                   float* ws, size_t ws_bytes, unsigned* err, int* splits_used);
 
 size_t attn_noalloc_ws_bytes();
 cudaError_t launch_attention_noalloc(cudaStream_t s, const AttnCompressed& k, const AttnCompressed& v,
