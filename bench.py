@@ -336,6 +336,71 @@ def run_attention(args):
             torch.cuda.empty_cache()
 
 
+def run_paged_kv(args):
+    """Paged compressed KV (config 5 shapes): decode attention over a paged
+    cache with a dense tail page, against the head-major kernel on the same
+    tokens, and the online append rate (one page per sequence and KV head)."""
+    import math
+
+    import torch
+
+    import zipserv_asplos26_b200 as zs
+    from zipserv_asplos26_b200.kvcache import PagedZipKVCache
+    dev = torch.device("cuda", 0)
+    peak, kind = peaks()
+    Hq, Hkv, D = 32, 8, 128
+    stream = torch.cuda.Stream(device=dev)
+    gen = torch.Generator(device=dev).manual_seed(9)
+
+    def kv(B, T):
+        scale = torch.exp(torch.empty(Hkv, D, device=dev).uniform_(math.log(0.1), math.log(4.0), generator=gen))
+        return (torch.randn(B, T, Hkv, D, device=dev, generator=gen) * scale).to(torch.bfloat16)
+
+    for B, T in ((32, 4096), (8, 16384), (1, 32768)):
+        k0, v0 = kv(B, T + 33), kv(B, T + 33)   # T + 33 tokens: the last page is a dense tail
+        blocks = (T + 64) // 64
+        cache = PagedZipKVCache(num_blocks=B * blocks, max_batch=B, max_blocks_per_seq=blocks, num_kv_heads=Hkv,
+                                k_window=PagedZipKVCache.window_from(k0[0]),
+                                v_window=PagedZipKVCache.window_from(v0[0]), full_elems_per_page=2048, device=dev)
+        for b in range(B):
+            cache.prefill(b, k0[b], v0[b])
+        q = torch.randn(B, Hq, D, device=dev, generator=gen).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        t_paged = _graph_time_us(torch, [lambda: cache.attention(q, out=out)] * 20, stream)
+        kc, vc = zs.compress_kv(k0), zs.compress_kv(v0)
+        seq = torch.full((B,), T + 33, dtype=torch.int32, device=dev)
+        t_head = _graph_time_us(torch, [lambda: zs.decode_attention(q, kc, vc, seq, Hkv, max_seqlen=T + 33,
+                                                                     out=out)] * 20, stream)
+        cb = int(cache.k.cursor[0].item() + 2 * cache.k.cursor[1].item() + cache.v.cursor[0].item()
+                 + 2 * cache.v.cursor[1].item()) + 2 * B * blocks * Hkv * (3 * 1024 + 64)
+        # append: one full page per sequence (B x Hkv pages of K and of V per launch)
+        xk, xv = kv(B, 64), kv(B, 64)
+        app = PagedZipKVCache(num_blocks=B * 8, max_batch=B, max_blocks_per_seq=8, num_kv_heads=Hkv,
+                              k_window=cache.k.top, v_window=cache.v.top, device=dev)
+        dst = torch.arange(B * Hkv, dtype=torch.int32, device=dev)
+        from zipserv_asplos26_b200.kvcache import _fn
+        import ctypes as C
+        f = _fn("zs_kv_append_pages")
+
+        def append_once():
+            app.k.cursor.zero_()
+            app.v.cursor.zero_()
+            for pool, x in ((app.k, xk), (app.v, xv)):
+                f(torch.cuda.current_stream().cuda_stream, C.byref(pool.st), x.data_ptr(), B, 1, Hkv, D,
+                  dst.data_ptr(), None)
+        t_app = _graph_time_us(torch, [append_once] * 20, stream)
+        print(json.dumps({"workload": "paged_kv", "B": B, "T": T + 33, "Hq": Hq, "Hkv": Hkv, "D": D,
+                          "paged_attention_us": round(t_paged, 2), "head_major_attention_us": round(t_head, 2),
+                          "paged_tok_per_s": round(B / (t_paged * 1e-6), 1),
+                          "paged_compressed_GBps": round(cb / t_paged / 1e3, 1),
+                          "paged_hbm_frac": round(cb / t_paged / 1e3 / peak, 4),
+                          "append_us_per_token_page": round(t_app, 2),
+                          "append_input_GBps": round(2 * 2 * B * 64 * Hkv * D / t_app / 1e3, 1),
+                          "peak": f"{peak} GB/s ({kind})"}), flush=True)
+        del cache, app, kc, vc, k0, v0
+        torch.cuda.empty_cache()
+
+
 def run_roundtrip(args):
     """Config 1: host TCA-TBE round trip of a 4096x4096 bf16 N(0, 0.02) matrix
     through the library's own host encoder and GPU decoder, plus GPU encode and
@@ -456,12 +521,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu", action="store_true", help="plain launches for ncu, no timing")
     ap.add_argument("--workload", default="config2",
-                    choices=["config2", "llama8b", "attention", "roundtrip", "tp70b"],
+                    choices=["config2", "llama8b", "attention", "roundtrip", "tp70b", "paged_kv"],
                     help="config2 = the headline line; the others print one JSON line per case")
     args = ap.parse_args()
     if args.workload != "config2" and args.impl == "ours" and not args.ncu:
         return {"llama8b": run_llama8b, "attention": run_attention, "roundtrip": run_roundtrip,
-                "tp70b": run_tp70b}[args.workload](args)
+                "tp70b": run_tp70b, "paged_kv": run_paged_kv}[args.workload](args)
     if args.impl == "reference":
         return run_reference(args)
     if args.ncu:
