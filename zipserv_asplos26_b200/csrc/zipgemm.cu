@@ -846,7 +846,9 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, int dev,
     if (!encode) return cudaErrorNotSupported;
     const int N = p.N;
     p.BN = (N + 15) / 16 * 16;
-    p.n_acc = (kTmemCols / (uint32_t)p.BN) >= 4 ? 4 : 2;   // accumulators of BN columns (power of two)
+    // accumulators of BN columns: the largest power of two <= 4 that fits in TMEM
+    p.n_acc = 4;
+    while (p.n_acc > 1 && (uint32_t)(p.n_acc * p.BN) > kTmemCols) p.n_acc >>= 1;
     p.gtk = p.K / kGT;
     p.mgt = p.M / kGT;
     const long long mtiles = (p.M + 127) / 128;
