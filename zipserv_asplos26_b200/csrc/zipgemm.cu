@@ -396,7 +396,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int4 f = uoffs[(i0 & 63) * 2 + sb], e = uoffs[((i0 + u) & 63) * 2 + sb];
                 cinfo[(s * kMaxChunk + u) * 2 + sb] = make_int2(max(e.x - f.x, 0), max(e.y - f.y, 0));
             }
-            const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, size) + (nsub == 2 ? fixed_bytes : fixed_bytes / 2);
+            uint32_t total = __reduce_add_sync(0xFFFFFFFFu, size) + (nsub == 2 ? fixed_bytes : fixed_bytes / 2);
+#ifdef ZS_TRACE
+            if (p.debug & 4) { total = 0; size = 0; }   // diagnostic: no weight traffic
+#endif
             __syncwarp();   // the chunk offsets above are released by lane 0's arrive
             uint64_t* bar = &hd->comp_full[s];
             if (lane == 0) {
@@ -406,7 +409,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             __syncwarp();
             uint8_t* slot = smem + p.off_c + (size_t)s * p.c_slot;
-            if (lane < 4) {
+            if (lane < 4 && total) {
                 ZS_GUARD(p.off_c + (uint32_t)s * p.c_slot + ldst + (lane < 3 ? 1024u : 64u) * (uint32_t)p.cu <= p.smem_bytes, 0x100)
                 tma_load_2d(slot + ldst, nsub == 2 ? lmap : lmap1, uc.kb * (lane < 3 ? 64 : 8), (int)(2 * T), bar);
             } else if (size) {
@@ -427,6 +430,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int kb = R.off0;
             for (int i = 0; i < R.n; ++i) {
                 if (rb.wrapped && !mbar_wait(&hd->b_empty[rb.slot], rb.phase ^ 1u, p.err, abort_flag)) break;
+                if (i < 14) ZS_STAMP(94 + i);
                 uint64_t* bar = &hd->b_full[rb.slot];
                 if (p.debug & 2) {
                     mbar_arrive(bar);
@@ -460,10 +464,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (first && racc.wrapped &&
                     !mbar_wait(&hd->acc_empty[racc.slot], racc.phase ^ 1u, p.err, abort_flag))
                     break;
-                if (!mbar_wait(&hd->a_full[sa], pa, p.err, abort_flag) ||
-                    !mbar_wait(&hd->b_full[sb], pb, p.err, abort_flag))
-                    break;
+                if (!mbar_wait(&hd->a_full[sa], pa, p.err, abort_flag)) break;
+                if (i < 14) ZS_STAMP(30 + i);
+                if (!mbar_wait(&hd->b_full[sb], pb, p.err, abort_flag)) break;
+                if (i < 14) ZS_STAMP(50 + i);
                 tc_fence_after();
+#ifdef ZS_TRACE
+                if (!(p.debug & 8))   // diagnostic: bit 8 skips the MMAs (commits still signal)
+#endif
                 ZS_GUARD(sa < p.na && sb < p.nb && racc.slot * p.BN + p.BN <= (int)kTmemCols, 0x10000) {
                     umma_bf16_ss(d, da, db, idesc, first ? 0u : 1u);
                     umma_bf16_ss(d, da + 2, db + 2, idesc, 1u);
@@ -646,7 +654,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     // a short chunk's missing units are accounted for by its first task
                     const uint32_t extra = (k == 0 && u == 0) ? (uint32_t)(kTasksPerUnit * (p.cu - clen)) : 0u;
                     mbar_arrive_cnt(&hd->comp_empty[cs], 1u + extra);
-                    if (k == 0 && i < 100) ZS_STAMP(10 + i);
+                    if (k == 0 && i < 20) ZS_STAMP(10 + i);
                 }
             }
             kb += UG;
