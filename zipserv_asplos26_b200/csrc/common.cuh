@@ -148,6 +148,32 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
     }
 }
 
+// Non-blocking test of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for two mbarrier phases. Both are tested back to back first, so when
+// both are already complete (the common case in a full pipeline) the two
+// round trips to the barrier unit overlap; otherwise each is waited for in turn.
+__device__ __forceinline__ bool mbar_wait2(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2, unsigned* err,
+                                           volatile int* abort_flag, bool sleep = false) {
+    const bool r1 = mbar_test(b1, p1);
+    const bool r2 = mbar_test(b2, p2);
+    if (r1 && r2) return true;
+    if (sleep)
+        return (r1 || mbar_wait_sleep(b1, p1, err, abort_flag)) && (r2 || mbar_wait_sleep(b2, p2, err, abort_flag));
+    return (r1 || mbar_wait(b1, p1, err, abort_flag)) && (r2 || mbar_wait(b2, p2, err, abort_flag));
+}
+
 // ------------------- programmatic dependent launch -------------------------
 // Wait until the preceding grid on the stream (launched before this one) has
 // completed and its memory operations are visible. A no-op without PDL.

@@ -464,9 +464,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (first && racc.wrapped &&
                     !mbar_wait(&hd->acc_empty[racc.slot], racc.phase ^ 1u, p.err, abort_flag))
                     break;
-                if (!mbar_wait(&hd->a_full[sa], pa, p.err, abort_flag)) break;
-                if (i < 14) ZS_STAMP(30 + i);
-                if (!mbar_wait(&hd->b_full[sb], pb, p.err, abort_flag)) break;
+                if (!mbar_wait2(&hd->a_full[sa], pa, &hd->b_full[sb], pb, p.err, abort_flag)) break;
                 if (i < 14) ZS_STAMP(50 + i);
                 tc_fence_after();
 #ifdef ZS_TRACE
@@ -608,13 +606,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // (the slot's previous fill has then landed and been consumed), after which the
                 // parity of the slot's barrier identifies the chunk exactly.
                 if (!wait_tag_at_least(&hd->ctag[cs], c, p.err, abort_flag)) break;
-                if (!mbar_wait_sleep(&hd->comp_full[cs], (uint32_t)((c >> p.lnc) & 1), p.err, abort_flag)) break;
-#ifdef ZS_TRACE
-                if (lane == 0 && warp == 0 && tq < 6) ZS_STAMP(71 + 4 * tq );
-#endif
-                if (i >= p.na &&
-                    !mbar_wait_sleep(&hd->a_empty[sa], (uint32_t)((around + 1) & 1), p.err, abort_flag))
+                // the unit's compressed chunk and a free A slot (the first na units have one)
+                if (i >= p.na) {
+                    if (!mbar_wait2(&hd->comp_full[cs], (uint32_t)((c >> p.lnc) & 1), &hd->a_empty[sa],
+                                    (uint32_t)((around + 1) & 1), p.err, abort_flag, true))
+                        break;
+                } else if (!mbar_wait_sleep(&hd->comp_full[cs], (uint32_t)((c >> p.lnc) & 1), p.err, abort_flag)) {
                     break;
+                }
 #ifdef ZS_TRACE
                 if (lane == 0 && warp == 0 && tq < 6) ZS_STAMP(72 + 4 * tq );
 #endif
