@@ -712,34 +712,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         ZS_STAMP(4 + 2 * which);
     }
     __syncthreads();
-    for (int which = 0; which < 2; ++which) {
-        if (fT[which] < 0 || !hd->go[which]) continue;
-        const long long T = fT[which];
-        const int ncon = fn[which], idx = fidx[which];
-        const int n0 = idx * p.BN / ncon, n1 = (idx + 1) * p.BN / ncon;
-        for (int e = tid; e < (n1 - n0) * 32; e += kGemmThreads) {
-            const int nl = n0 + (e >> 5), m4 = (e & 31) * 4;
-            const float* base = p.ws + (size_t)nl * 128 + m4;
-            const size_t cstride = 2 * (size_t)p.BN * 128;
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-            // contributors in CTA order, four loads in flight at a time
-            for (int c0 = 0; c0 < ncon; c0 += 4) {
-                float4 v[4];
+    {
+        // This CTA's column slices of both split tiles form one list of float4
+        // items (32 per column), so every thread has at most a few items and all
+        // contributors' loads of an item (eight at a time) are in flight at once.
+        // Contributors are summed in CTA order, so the result is deterministic.
+        int sn0[2], slen[2];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
+        for (int which = 0; which < 2; ++which) {
+            const bool on = fT[which] >= 0 && hd->go[which];
+            const int ncon = on ? fn[which] : 1, idx = on ? fidx[which] : 0;
+            sn0[which] = idx * p.BN / ncon;
+            slen[which] = on ? ((idx + 1) * p.BN / ncon - sn0[which]) * 32 : 0;
+        }
+        const size_t cstride = 2 * (size_t)p.BN * 128;
+        for (int e = tid; e < slen[0] + slen[1]; e += kGemmThreads) {
+            const bool w1 = e >= slen[0];   // second split tile (selects keep the arrays in registers)
+            const int el = w1 ? e - slen[0] : e;
+            const int ncon = w1 ? fn[1] : fn[0];
+            const long long cf = w1 ? fcf[1] : fcf[0], Tw = w1 ? fT[1] : fT[0];
+            const int nl = (w1 ? sn0[1] : sn0[0]) + (el >> 5), m4 = (el & 31) * 4;
+            const float* base = p.ws + (size_t)nl * 128 + m4 + (size_t)cf * cstride;
+            const size_t first = (size_t)(w1 ? fslot0[1] : fslot0[0]) * p.BN * 128;
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int c0 = 0; c0 < ncon; c0 += 8) {
+                float4 v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
                     v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
                     const int cc = c0 + j;
                     if (cc < ncon) {
-                        const size_t off = (size_t)(fcf[which] + cc) * cstride +
-                                           (cc == 0 ? (size_t)fslot0[which] * p.BN * 128 : 0);
-                        ZS_GUARD(off + (size_t)nl * 128 + m4 + 4 <= p.ws_floats, 0x4000)
+                        const size_t off = (size_t)cc * cstride + (cc == 0 ? first : 0);
+                        ZS_GUARD((size_t)cf * cstride + off + (size_t)nl * 128 + m4 + 4 <= p.ws_floats, 0x4000)
                         v[j] = __ldcg(reinterpret_cast<const float4*>(base + off));
                     }
                 }
 #pragma unroll
-                for (int j = 0; j < 4; ++j) { a.x += v[j].x; a.y += v[j].y; a.z += v[j].z; a.w += v[j].w; }
+                for (int j = 0; j < 8; ++j) { a.x += v[j].x; a.y += v[j].y; a.z += v[j].z; a.w += v[j].w; }
             }
-            const int m = (int)(T * 128) + m4;
+            const int m = (int)(Tw * 128) + m4;
             if (nl < p.N && m < p.M) {
                 __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
                 uint2 pk;
