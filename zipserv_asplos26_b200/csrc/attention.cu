@@ -89,9 +89,9 @@ struct AttnSmem {
     float mm[kAttnMaxG], ml[kAttnMaxG];
 };
 
-// ---------------- legacy tensor-core helpers for the small attention math ----------------
+// ---------------- warp-level tensor-core helpers for the small attention math ----------------
 // (G <= 8 query heads per page: far too small for tcgen05 tiles; mma.sync m16n8k16 with the
-// heads in rows 0..7 and ldmatrix from the decoded, 128-byte-swizzled page tiles.)
+// heads in the 8 columns and ldmatrix from the decoded, 128-byte-swizzled page tiles.)
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -102,14 +102,20 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
 }
-// d[0..1] += A(rows 0-7: a0 / a2, rows 8-15 zero) * B; the zero rows' results are dropped.
-__device__ __forceinline__ void mma_rows8(float& d0, float& d1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-    float x2, x3;
+// d[0..3] += A (16x16, row) * B (16x8, col), bf16 in, fp32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %10, %10};"
-        : "+f"(d0), "+f"(d1), "=f"(x2), "=f"(x3)
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(0.f));
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Transpose an 8x8 b16 matrix held in the m8n8 fragment layout across the warp.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
 }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -122,9 +128,11 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 //                fetched one page ahead
 //   warps 0-15   decoders: warp w always decodes median tile w % 4 of GT (w / 4) % 2
 //                of K (w < 8) or V into the page's 128-byte-swizzled bf16 tiles
-//   warps 17-18  math on alternate pages: S = Q K^T and O += P V with mma.sync
-//                (K fragments by ldmatrix, V by ldmatrix.trans; P reuses the S
-//                accumulator registers as the A operand), online base-2 softmax
+//   warps 17-18  math on alternate pages with mma.sync m16n8k16: S^T = K Q^T
+//                (tokens in the tile rows, query heads in its 8 columns, K by
+//                ldmatrix), online base-2 softmax per head column, then
+//                O^T += V^T P^T (head dims in the rows, V by ldmatrix.trans,
+//                P^T from the S^T accumulators by movmatrix.trans)
 // The two math warps merge (m, l, O) at the end; with S > 1 splits the CTA writes
 // (m, l, unnormalised O) to the workspace for attn_combine_kernel.
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const AttnParams p) {
@@ -288,101 +296,110 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             if (++s == p.nslots) { s = 0; ph ^= 1u; }
         }
     } else {
-        // math warps: rows of the mma tiles = query heads (group = lane / 4 < G)
+        // Math warps, one page each in turn. The m16n8k16 tiles put the page's
+        // tokens (S^T = K Q^T) or head dims (O^T = V^T P^T) in the 16 rows and
+        // the G <= 8 query heads in the 8 columns, so no MMA row is padding.
+        // Lane (g = lane / 4, t4 = lane % 4) holds heads 2 t4 and 2 t4 + 1;
+        // movmatrix turns the S^T accumulator layout into the P^T operand.
         const int mw = warp - kAttnMath0;
-        const int grp = lane >> 2, t4 = lane & 3;
-        float o[16][2];
+        const int g8 = lane >> 2, t4 = lane & 3;
+        // Q^T B fragments for the 8 k-steps of 16 dims (rows of heads >= G are zero)
+        uint32_t qb[8][2];
 #pragma unroll
-        for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = 0.f;
-        float m_run = -INFINITY, l_run = 0.f;
+        for (int ks = 0; ks < 8; ++ks) {
+            qb[ks][0] = *reinterpret_cast<const uint32_t*>(&A.qs[g8][16 * ks + 2 * t4]);
+            qb[ks][1] = *reinterpret_cast<const uint32_t*>(&A.qs[g8][16 * ks + 8 + 2 * t4]);
+        }
+        float o[8][4];   // O^T: dim tile dt, rows g8 / g8 + 8, heads 2 t4 / 2 t4 + 1
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
+        float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+        const int lr = (lane & 7) + 8 * ((lane >> 3) & 1), lc = lane >> 4;   // ldmatrix row / 8-column half (K)
+        const int vr = (lane & 7) + 8 * (lane >> 4), vc = (lane >> 3) & 1;    // ldmatrix.trans token / dim half (V)
         int s = mw % p.nslots, kround = mw / p.nslots;   // page pi = mw + 2j: tile slot pi % n, round pi / n
         for (int pi = mw; pi < np; pi += 2) {
             if (!mbar_wait(&A.tfull[s], (uint32_t)(kround & 1), p.err, abort_flag)) break;
             const uint32_t kt = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes, vt = kt + 16384u;
-            // S = Q K^T over the page's 64 tokens (8 n-tiles of 8 tokens)
-            float sc[8][2];
+            // S^T = K Q^T: 4 token tiles x 8 dim steps
+            float sc[4][4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = 0.f;
-            const int mi = lane >> 3, rr = lane & 7;
-            // lane's row address in the Q tile for ldmatrix: matrix mi = (k-step 2 k2 + mi / 2, dims half mi % 2)
-            const uint32_t qbase = smem_u32(&A.qs[rr][0]) + 16u * (uint32_t)mi;
+            for (int mt = 0; mt < 4; ++mt) {
+                sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+                const uint32_t tok = 16u * (uint32_t)mt + (uint32_t)lr;
 #pragma unroll
-            for (int jp = 0; jp < 4; ++jp) {
-                const uint32_t tok = 8u * (uint32_t)(2 * jp + (mi >> 1)) + (uint32_t)rr;
-#pragma unroll
-                for (int k2 = 0; k2 < 4; ++k2) {
-                    // Q A-fragments of k-steps 2 k2 and 2 k2 + 1 (rows 0-7 = query heads)
-                    uint32_t q0, q1, q2, q3;
-                    ldsm_x4(qbase + 64u * (uint32_t)k2, q0, q1, q2, q3);
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; ++h2) {
-                        const int kk = 2 * k2 + h2;
-                        const uint32_t chunk = 2u * (uint32_t)(kk & 3) + (uint32_t)(mi & 1);
-                        const uint32_t addr =
-                            kt + 8192u * (uint32_t)(kk >> 2) + tok * 128u + ((chunk ^ (tok & 7u)) << 4);
-                        uint32_t b0, b1, b2, b3;
-                        ldsm_x4(addr, b0, b1, b2, b3);
-                        const uint32_t a0 = h2 ? q2 : q0, a2 = h2 ? q3 : q1;
-                        mma_rows8(sc[2 * jp][0], sc[2 * jp][1], a0, a2, b0, b1);
-                        mma_rows8(sc[2 * jp + 1][0], sc[2 * jp + 1][1], a0, a2, b2, b3);
-                    }
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint32_t chunk = 2u * (uint32_t)(ks & 3) + (uint32_t)lc;
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(kt + 8192u * (uint32_t)(ks >> 2) + tok * 128u + ((chunk ^ (tok & 7u)) << 4), a0, a1, a2, a3);
+                    mma_16816(sc[mt], a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
                 }
             }
-            // online softmax of row grp (tokens 8j + 2 t4 + e of this page)
+            // online softmax per head column over the page's 64 tokens
             const int tok0 = (pg0 + pi) * 64;
-            float mx = -INFINITY;
+            float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
+            for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int t = tok0 + 8 * j + 2 * t4 + e;
-                    const float x = t < len ? sc[j][e] * p.scale_log2 : -INFINITY;
-                    sc[j][e] = x;
-                    mx = fmaxf(mx, x);
+                for (int e = 0; e < 4; ++e) {
+                    const int t = tok0 + 16 * mt + g8 + 8 * (e >> 1);
+                    const float x = t < len ? sc[mt][e] * p.scale_log2 : -INFINITY;
+                    sc[mt][e] = x;
+                    mx[e & 1] = fmaxf(mx[e & 1], x);
                 }
-            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
-            const float m_new = fmaxf(m_run, mx);
-            const float mref = m_new == -INFINITY ? 0.f : m_new;
-            const float alpha = exp2f(m_run - mref);
-            float sum = 0.f;
+            float alpha[2], mref[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xFFFFFFFFu, mx[h], 4));
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xFFFFFFFFu, mx[h], 8));
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xFFFFFFFFu, mx[h], 16));
+                const float m_new = fmaxf(m_run[h], mx[h]);
+                mref[h] = m_new == -INFINITY ? 0.f : m_new;
+                alpha[h] = exp2f(m_run[h] - mref[h]);
+                m_run[h] = m_new;
+            }
             // P as a bf16 pair hi + lo (lo = the rounding residual) so that P.V keeps
-            // ~16 bits of P: two mma per fragment instead of one
-            uint32_t pa0[4], pa2[4], pl0[4], pl2[4];
+            // about 16 bits of P; movmatrix.trans makes each 8x8 block a P^T fragment
+            uint32_t ph[4][2], pl[4][2];
+            float sum[2] = {0.f, 0.f};
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float e0 = exp2f(sc[j][0] - mref), e1 = exp2f(sc[j][1] - mref);
-                sum += e0 + e1;
-                const __nv_bfloat162 hi = __floats2bfloat162_rn(e0, e1);
-                const float2 hf = __bfloat1622float2(hi);
-                const uint32_t h = *reinterpret_cast<const uint32_t*>(&hi), l = pack_bf16(e0 - hf.x, e1 - hf.y);
-                if (j & 1) { pa2[j >> 1] = h; pl2[j >> 1] = l; }
-                else { pa0[j >> 1] = h; pl0[j >> 1] = l; }
+            for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    const float e0 = exp2f(sc[mt][2 * r] - mref[0]), e1 = exp2f(sc[mt][2 * r + 1] - mref[1]);
+                    sum[0] += e0;
+                    sum[1] += e1;
+                    const __nv_bfloat162 hi = __floats2bfloat162_rn(e0, e1);
+                    const float2 hf = __bfloat1622float2(hi);
+                    ph[mt][r] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&hi));
+                    pl[mt][r] = movmatrix_trans(pack_bf16(e0 - hf.x, e1 - hf.y));
+                }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                sum[h] += __shfl_xor_sync(0xFFFFFFFFu, sum[h], 4);
+                sum[h] += __shfl_xor_sync(0xFFFFFFFFu, sum[h], 8);
+                sum[h] += __shfl_xor_sync(0xFFFFFFFFu, sum[h], 16);
+                l_run[h] = l_run[h] * alpha[h] + sum[h];
             }
-            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
-            l_run = l_run * alpha + sum;
-            m_run = m_new;
 #pragma unroll
-            for (int n = 0; n < 16; ++n) {
-                o[n][0] *= alpha;
-                o[n][1] *= alpha;
+            for (int dt = 0; dt < 8; ++dt) {
+                o[dt][0] *= alpha[0];
+                o[dt][1] *= alpha[1];
+                o[dt][2] *= alpha[0];
+                o[dt][3] *= alpha[1];
             }
-            // O += P V: 16 n-tiles of 8 dims, 4 k-steps of 16 tokens
+            // O^T += V^T P^T: 8 dim tiles x 4 token steps (hi and lo parts of P)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const uint32_t tok = 16u * (uint32_t)kk + 8u * (uint32_t)(mi & 1) + (uint32_t)rr;
+            for (int ks = 0; ks < 4; ++ks) {
+                const uint32_t tok = 16u * (uint32_t)ks + (uint32_t)vr;
 #pragma unroll
-                for (int np2 = 0; np2 < 8; ++np2) {
-                    const uint32_t dc = 2u * (uint32_t)np2 + (uint32_t)(mi >> 1);   // 8-dim chunk 0..15
-                    const uint32_t addr = vt + 8192u * (dc >> 3) + tok * 128u + (((dc & 7u) ^ (tok & 7u)) << 4);
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4_t(addr, b0, b1, b2, b3);
-                    mma_rows8(o[2 * np2][0], o[2 * np2][1], pa0[kk], pa2[kk], b0, b1);
-                    mma_rows8(o[2 * np2 + 1][0], o[2 * np2 + 1][1], pa0[kk], pa2[kk], b2, b3);
+                for (int dt = 0; dt < 8; ++dt) {
+                    const uint32_t chunk = 2u * (uint32_t)(dt & 3) + (uint32_t)vc;
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(vt + 8192u * (uint32_t)(dt >> 2) + tok * 128u + ((chunk ^ (tok & 7u)) << 4), a0, a1, a2,
+                              a3);
+                    mma_16816(o[dt], a0, a1, a2, a3, ph[ks][0], ph[ks][1]);
 #if ZS_ATTN_P_SPLIT
-                    mma_rows8(o[2 * np2][0], o[2 * np2][1], pl0[kk], pl2[kk], b0, b1);
-                    mma_rows8(o[2 * np2 + 1][0], o[2 * np2 + 1][1], pl0[kk], pl2[kk], b2, b3);
+                    mma_16816(o[dt], a0, a1, a2, a3, pl[ks][0], pl[ks][1]);
 #endif
                 }
             }
@@ -391,45 +408,53 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             s += 2;
             while (s >= p.nslots) { s -= p.nslots; ++kround; }
         }
-        // merge the two math warps: warp 18 publishes, warp 17 combines and writes
+        // merge the two math warps: warp kAttnMath0 + 1 publishes, kAttnMath0 combines and writes
         if (mw == 1) {
-            if (grp < G) {
 #pragma unroll
-                for (int n = 0; n < 16; ++n) {
-                    A.mo[grp][8 * n + 2 * t4] = o[n][0];
-                    A.mo[grp][8 * n + 2 * t4 + 1] = o[n][1];
-                }
-                if (t4 == 0) { A.mm[grp] = m_run; A.ml[grp] = l_run; }
+            for (int dt = 0; dt < 8; ++dt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) A.mo[2 * t4 + (e & 1)][16 * dt + g8 + 8 * (e >> 1)] = o[dt][e];
+            if (g8 == 0) {
+                A.mm[2 * t4] = m_run[0]; A.mm[2 * t4 + 1] = m_run[1];
+                A.ml[2 * t4] = l_run[0]; A.ml[2 * t4 + 1] = l_run[1];
             }
         }
         asm volatile("bar.sync 1, 64;" ::: "memory");
-        if (mw == 0 && grp < G) {
-            const float m1 = A.mm[grp], l1 = A.ml[grp];
-            const float M = fmaxf(m_run, m1);
-            const float Mref = M == -INFINITY ? 0.f : M;
-            const float s0 = exp2f(m_run - Mref), s1 = exp2f(m1 - Mref);
-            const float L = l_run * s0 + l1 * s1;
-            const int hq = hk * G + grp;
-            if (p.S == 1) {
-                const float inv = L > 0.f ? 1.f / L : 0.f;
+        if (mw == 0) {
+            float s0[2], s1[2], Mh[2], Lh[2];
 #pragma unroll
-                for (int n = 0; n < 16; ++n) {
-                    const int d = 8 * n + 2 * t4;
-                    const float v0 = (o[n][0] * s0 + A.mo[grp][d] * s1) * inv;
-                    const float v1 = (o[n][1] * s0 + A.mo[grp][d + 1] * s1) * inv;
-                    *reinterpret_cast<uint32_t*>(&p.out[((size_t)b * p.Hq + hq) * kAttnD + d]) = pack_bf16(v0, v1);
-                }
-            } else {
-                float* w = p.ws + (((size_t)bh * p.S + split) * G + grp) * (kAttnD + 2);
+            for (int h = 0; h < 2; ++h) {
+                const int hh = 2 * t4 + h;
+                const float m1 = A.mm[hh], l1 = A.ml[hh];
+                Mh[h] = fmaxf(m_run[h], m1);
+                const float Mref = Mh[h] == -INFINITY ? 0.f : Mh[h];
+                s0[h] = exp2f(m_run[h] - Mref);
+                s1[h] = exp2f(m1 - Mref);
+                Lh[h] = l_run[h] * s0[h] + l1 * s1[h];
+            }
 #pragma unroll
-                for (int n = 0; n < 16; ++n) {
-                    const int d = 8 * n + 2 * t4;
-                    w[d] = o[n][0] * s0 + A.mo[grp][d] * s1;
-                    w[d + 1] = o[n][1] * s0 + A.mo[grp][d + 1] * s1;
+            for (int dt = 0; dt < 8; ++dt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int h = e & 1, hh = 2 * t4 + h, d = 16 * dt + g8 + 8 * (e >> 1);
+                    if (hh >= G) continue;
+                    const float v = o[dt][e] * s0[h] + A.mo[hh][d] * s1[h];
+                    if (p.S == 1) {
+                        const float inv = Lh[h] > 0.f ? 1.f / Lh[h] : 0.f;
+                        p.out[((size_t)b * p.Hq + hk * G + hh) * kAttnD + d] =
+                            __bfloat16_as_ushort(__float2bfloat16_rn(v * inv));
+                    } else {
+                        p.ws[(((size_t)bh * p.S + split) * G + hh) * (kAttnD + 2) + d] = v;
+                    }
                 }
-                if (t4 == 0) {
-                    w[kAttnD] = M;
-                    w[kAttnD + 1] = L;
+            if (p.S > 1 && g8 == 0) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int hh = 2 * t4 + h;
+                    if (hh >= G) continue;
+                    float* w = p.ws + (((size_t)bh * p.S + split) * G + hh) * (kAttnD + 2);
+                    w[kAttnD] = Mh[h];
+                    w[kAttnD + 1] = Lh[h];
                 }
             }
         }
