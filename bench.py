@@ -383,8 +383,8 @@ def run_paged_kv(args):
         f = _fn("zs_kv_append_pages")
 
         def append_once():
-            app.k.cursor.zero_()
-            app.v.cursor.zero_()
+            app.k.cursor[:2].zero_()
+            app.v.cursor[:2].zero_()
             for pool, x in ((app.k, xk), (app.v, xv)):
                 f(torch.cuda.current_stream().cuda_stream, C.byref(pool.st), x.data_ptr(), B, 1, Hkv, D,
                   dst.data_ptr(), None)

@@ -131,7 +131,8 @@ typedef struct ZsKvPool {
     uint64_t* d_b1, *d_b2, *d_b3;  /* [num_pages * 2 * 64] bitmaps */
     int* d_mt_off;                 /* [num_pages * 2 * 8] median-tile offsets */
     int* d_page_off;               /* [num_pages * 6]: {hf, fallback} starts of GT 0, GT 1 and the end */
-    unsigned long long* d_cursor;  /* [2]: next free hf byte, next free fallback element (start at 0) */
+    unsigned long long* d_cursor;  /* [4] (start at 0): next free hf byte, next free fallback element, and the
+                                      largest padded hf / fallback length of a GT appended so far */
     int64_t hf_capacity, full_capacity;
     int num_pages;                 /* num_blocks * Hkv */
     int start_exp;                 /* (top[0] - 1) mod 256 of the window below */

@@ -77,7 +77,36 @@ struct AttnParams {
     int max_blocks, num_blocks;
     const uint16_t* tail_k;
     const uint16_t* tail_v;
+    // Paged pools' running maxima of a GT's padded {hf bytes, fallback elements}
+    // (nullable): when given, every CTA sizes its page slots from them and
+    // fits as many (2 or 3) as the launch's shared memory allows.
+    const unsigned long long* k_max;
+    const unsigned long long* v_max;
+    uint32_t smem_bytes;
 };
+
+// Shared-memory carve-up of the page rings (from the host, or from the pools'
+// device-side maxima in the paged layout).
+struct AttnLayout {
+    uint32_t c_hf, hf_cap, c_full, full_cap, c_mat, c_slot, off_slots;
+    int nslots;
+};
+
+__device__ __forceinline__ AttnLayout attn_layout(const AttnParams& p) {
+    AttnLayout L{p.c_hf, p.hf_cap, p.c_full, p.full_cap, p.c_mat, p.c_slot, p.off_slots, p.nslots};
+    if (p.k_max) {
+        const unsigned long long mh = max(p.k_max[0], p.v_max[0]), mf = max(p.k_max[1], p.v_max[1]);
+        const uint32_t hfc = (uint32_t)min(mh, 4096ull + 16), ffc = (uint32_t)min(mf, 4096ull + 8) * 2u;
+        L.hf_cap = 2u * ((hfc + 15u) & ~15u);
+        L.c_full = L.c_hf + L.hf_cap + 16u;
+        L.full_cap = 2u * ((ffc + 15u) & ~15u);
+        L.c_mat = (L.c_full + L.full_cap + 16u + 127u) & ~127u;
+        L.c_slot = 2u * L.c_mat;
+        L.nslots = p.off_tiles + 3u * (kAttnTileBytes + L.c_slot) <= p.smem_bytes ? 3 : 2;
+        L.off_slots = p.off_tiles + (uint32_t)L.nslots * kAttnTileBytes;
+    }
+    return L;
+}
 
 struct AttnSmem {
     uint64_t cfull[kAttnSlots], cempty[kAttnSlots];
@@ -139,6 +168,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
     extern __shared__ __align__(1024) uint8_t smem[];
     AttnSmem& A = *reinterpret_cast<AttnSmem*>(smem);
     const uint32_t smem0 = smem_u32(smem);
+    const AttnLayout L = attn_layout(p);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh = blockIdx.x, split = blockIdx.y;
@@ -158,7 +188,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
         A.qs[h][d] = h < G ? p.q[((size_t)b * p.Hq + hk * G + h) * kAttnD + d] : (uint16_t)0;
     }
     if (tid == 0) {
-        for (int s = 0; s < p.nslots; ++s) {
+        for (int s = 0; s < L.nslots; ++s) {
             mbar_init(&A.cfull[s], 1);
             mbar_init(&A.cempty[s], kAttnDecWarps);
             mbar_init(&A.tfull[s], kAttnDecWarps);
@@ -203,14 +233,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
         bool ok = true;
         for (int pi = 0; pi < np && ok; ++pi) {
             const PageRec nxt = fetch(pi + 1);   // in flight while this page is issued
-            if (lane == 0 && pi >= p.nslots) ok = mbar_wait(&A.cempty[s], ph ^ 1u, p.err, abort_flag);
+            if (lane == 0 && pi >= L.nslots) ok = mbar_wait(&A.cempty[s], ph ^ 1u, p.err, abort_flag);
             ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             const int mb = 3 * mat;
             const int h0 = __shfl_sync(0xFFFFFFFFu, cur.e.x, mb), f0 = __shfl_sync(0xFFFFFFFFu, cur.e.y, mb);
             const int h1 = __shfl_sync(0xFFFFFFFFu, cur.e.x, mb + 1), f1 = __shfl_sync(0xFFFFFFFFu, cur.e.y, mb + 1);
             const int h2 = __shfl_sync(0xFFFFFFFFu, cur.e.x, mb + 2), f2 = __shfl_sync(0xFFFFFFFFu, cur.e.y, mb + 2);
-            uint8_t* slot = smem + p.off_slots + (size_t)s * p.c_slot + (size_t)mat * p.c_mat;
+            uint8_t* slot = smem + L.off_slots + (size_t)s * L.c_slot + (size_t)mat * L.c_mat;
             const long long gt0 = cur.gt0;
             uint32_t size = 0, dst = 0;
             const void* src = nullptr;
@@ -226,7 +256,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
                 } else {
                     const bool hf = kind == 4;
                     const int beg = hf ? h0 : f0, end = hf ? h2 : f2;
-                    const uint32_t esz = hf ? 1u : 2u, cap = hf ? p.hf_cap : p.full_cap;
+                    const uint32_t esz = hf ? 1u : 2u, cap = hf ? L.hf_cap : L.full_cap;
                     const int al = hf ? 16 : 8;
                     uint32_t bytes = end > beg ? (uint32_t)(end - beg) * esz : 0u;
                     int bg = beg;
@@ -236,7 +266,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
                         bg = max(bg, 0) & ~(al - 1);
                     }
                     size = bytes;
-                    dst = hf ? p.c_hf : p.c_full;
+                    dst = hf ? L.c_hf : L.c_full;
                     src = hf ? (const void*)(S.sm + bg) : (const void*)(S.full + bg);
                 }
             }
@@ -248,7 +278,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             __syncwarp();
             if (size) bulk_g2s(slot + dst, src, size, &A.cfull[s]);
             cur = nxt;
-            if (++s == p.nslots) { s = 0; ph ^= 1u; }
+            if (++s == L.nslots) { s = 0; ph ^= 1u; }
         }
     } else if (warp < kAttnDecWarps) {
         const int mat = warp >> 3, gc = (warp >> 2) & 1, mtile = warp & 3;
@@ -258,18 +288,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
         for (int pi = 0; pi < np; ++pi) {
             if (*abort_flag) break;
             if (!mbar_wait_sleep(&A.cfull[s], ph, p.err, abort_flag)) break;
-            if (pi >= p.nslots && !mbar_wait_sleep(&A.tempty[s], ph ^ 1u, p.err, abort_flag)) break;
-            const uint32_t base = launder(smem0 + p.off_slots + (uint32_t)s * p.c_slot + (uint32_t)mat * p.c_mat);
+            if (pi >= L.nslots && !mbar_wait_sleep(&A.tempty[s], ph ^ 1u, p.err, abort_flag)) break;
+            const uint32_t base = launder(smem0 + L.off_slots + (uint32_t)s * L.c_slot + (uint32_t)mat * L.c_mat);
             const int2 inf = gc ? A.info[s][mat] : make_int2(0, 0);
-            const uint32_t h0 = min((uint32_t)inf.x, p.hf_cap), f0 = min((uint32_t)inf.y, p.full_cap / 2);
+            const uint32_t h0 = min((uint32_t)inf.x, L.hf_cap), f0 = min((uint32_t)inf.y, L.full_cap / 2);
             GtView g;
             g.bm = base + 512u * (uint32_t)gc;
             g.bstride = 1024u;
             g.mt = base + 3072u + 32u * (uint32_t)gc;
-            g.sm = base + p.c_hf + h0;
-            g.full = base + p.c_full + 2u * f0;
-            g.hf_cap = p.hf_cap - h0;
-            g.full_cap = p.full_cap / 2 - f0;
+            g.sm = base + L.c_hf + h0;
+            g.full = base + L.c_full + 2u * f0;
+            g.hf_cap = L.hf_cap - h0;
+            g.full_cap = L.full_cap / 2 - f0;
             const uint32_t rows = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes + 16384u * (uint32_t)mat +
                                   8192u * (uint32_t)gc + 2048u * (uint32_t)mtile;
             if (is_dense_page(pg0 + pi)) {
@@ -293,7 +323,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
                 mbar_arrive(&A.tfull[s]);
                 mbar_arrive(&A.cempty[s]);
             }
-            if (++s == p.nslots) { s = 0; ph ^= 1u; }
+            if (++s == L.nslots) { s = 0; ph ^= 1u; }
         }
     } else {
         // Math warps, one page each in turn. The m16n8k16 tiles put the page's
@@ -316,7 +346,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
         float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
         const int lr = (lane & 7) + 8 * ((lane >> 3) & 1), lc = lane >> 4;   // ldmatrix row / 8-column half (K)
         const int vr = (lane & 7) + 8 * (lane >> 4), vc = (lane >> 3) & 1;    // ldmatrix.trans token / dim half (V)
-        int s = mw % p.nslots, kround = mw / p.nslots;   // page pi = mw + 2j: tile slot pi % n, round pi / n
+        int s = mw % L.nslots, kround = mw / L.nslots;   // page pi = mw + 2j: tile slot pi % n, round pi / n
         for (int pi = mw; pi < np; pi += 2) {
             if (!mbar_wait(&A.tfull[s], (uint32_t)(kround & 1), p.err, abort_flag)) break;
             const uint32_t kt = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes, vt = kt + 16384u;
@@ -406,7 +436,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             __syncwarp();
             if (lane == 0) mbar_arrive(&A.tempty[s]);
             s += 2;
-            while (s >= p.nslots) { s -= p.nslots; ++kround; }
+            while (s >= L.nslots) { s -= L.nslots; ++kround; }
         }
         // merge the two math warps: warp kAttnMath0 + 1 publishes, kAttnMath0 combines and writes
         if (mw == 1) {
@@ -548,6 +578,8 @@ static cudaError_t attention_core(cudaStream_t stream, const AttnCompressed& kc,
         p.num_blocks = pg->num_blocks;
         p.tail_k = pg->tail_k;
         p.tail_v = pg->tail_v;
+        p.k_max = pg->k_max;
+        p.v_max = pg->v_max;
     }
     p.q = q; p.seqlens = seqlens; p.out = out; p.ws = ws; p.err = err;
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.T_pad = T_pad; p.S = S;
@@ -573,8 +605,12 @@ static cudaError_t attention_core(cudaStream_t stream, const AttnCompressed& kc,
     while (p.nslots > 2 && p.off_tiles + (uint32_t)p.nslots * (kAttnTileBytes + p.c_slot) > (uint32_t)max_smem)
         --p.nslots;
     p.off_slots = p.off_tiles + (uint32_t)p.nslots * kAttnTileBytes;
-    const uint32_t smem_bytes = p.off_slots + (uint32_t)p.nslots * p.c_slot;
+    uint32_t smem_bytes = p.off_slots + (uint32_t)p.nslots * p.c_slot;
     if (smem_bytes > (uint32_t)max_smem) return cudaErrorInvalidValue;
+    // with the pools' device-side maxima the kernel sizes its own page slots
+    // (the worst case above fits two), so it gets all the shared memory there is
+    if (p.k_max) smem_bytes = (uint32_t)max_smem;
+    p.smem_bytes = smem_bytes;
     ZS_RETURN_IF_ERR(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem_bytes));
     attn_decode_kernel<<<dim3((unsigned)(B * Hkv), (unsigned)S), kAttnThreads, smem_bytes, stream>>>(p);

@@ -167,6 +167,8 @@ extern "C" int zs_decode_attention_paged(void* stream, const uint16_t* d_q, cons
     pg.v_page_off = v->d_page_off;
     pg.tail_k = d_tail_k;
     pg.tail_v = d_tail_v;
+    pg.k_max = k->d_cursor + 2;
+    pg.v_max = v->d_cursor + 2;
     return zs::launch_attention_paged((cudaStream_t)stream, pool_view(*k), pool_view(*v), pg, d_q, d_seqlens, d_out,
                                       B, Hq, Hkv, D, max_seqlen, softmax_scale, num_splits, d_ws, ws_bytes, d_err,
                                       splits_used);

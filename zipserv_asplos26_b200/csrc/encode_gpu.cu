@@ -409,7 +409,8 @@ __global__ void __launch_bounds__(128) encode_kernel(const uint16_t* __restrict_
 // bitmap / median-offset slots 2P and 2P+1; its streams are appended to the
 // pools at positions taken from the pool cursors (one atomic per stream and
 // page, so the two GTs' streams are contiguous) and recorded in
-// page_off[6P .. 6P+5] = {hf, fallback} starts of GT 0 and GT 1, and the end.
+// page_off[6P .. 6P+5] = {hf, fallback} starts of GT 0 and GT 1, and the end;
+// cursor[2], cursor[3] keep the largest padded hf and fallback length of a GT.
 // A page that does not fit in the pools sets kErrStreamOverflow and records
 // an empty page.
 __global__ void __launch_bounds__(256) kv_append_kernel(const uint16_t* __restrict__ x, int Hkv,
@@ -446,6 +447,9 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const uint16_t* __restri
         const bool ok = hb + ph0 + ph1 <= hf_cap && fb + pf0 + pf1 <= full_cap && hb + ph0 + ph1 <= 0x7FFFFFFFll &&
                         fb + pf0 + pf1 <= 0x7FFFFFFFll;
         int* po = page_off + 6LL * P;
+        // running maxima of a GT's padded stream lengths (decode attention sizes its slots from them)
+        atomicMax(&cursor[2], (unsigned long long)max(ph0, ph1));
+        atomicMax(&cursor[3], (unsigned long long)max(pf0, pf1));
         if (ok) {
             base[0] = hb;
             base[1] = fb;

@@ -72,6 +72,10 @@ struct AttnPaged {
     const int* v_page_off;
     const uint16_t* tail_k;
     const uint16_t* tail_v;
+    // nullable: {max padded hf bytes, max padded fallback elements} of a GT in
+    // each pool, kept by the append kernel; lets the kernel size its page slots
+    const unsigned long long* k_max;
+    const unsigned long long* v_max;
 };
 
 cudaError_t launch_attention_paged(cudaStream_t s, const AttnCompressed& k, const AttnCompressed& v,

@@ -98,7 +98,7 @@ class _Pool:
         self.b = [torch.zeros(num_pages * 2 * 64, dtype=torch.uint64, device=device) for _ in range(3)]
         self.mt_off = torch.zeros(num_pages * 2 * 8, dtype=torch.int32, device=device)
         self.page_off = torch.zeros(num_pages * 6, dtype=torch.int32, device=device)
-        self.cursor = torch.zeros(2, dtype=torch.int64, device=device)
+        self.cursor = torch.zeros(4, dtype=torch.int64, device=device)   # next hf, next fallback, max hf, max fallback per GT
         self.st = ZsKvPool(self.sm.data_ptr(), self.full.data_ptr(), self.b[0].data_ptr(), self.b[1].data_ptr(),
                            self.b[2].data_ptr(), self.mt_off.data_ptr(), self.page_off.data_ptr(),
                            self.cursor.data_ptr(), hf_bytes, full_elems, num_pages, self.start_exp,
