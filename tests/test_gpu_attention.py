@@ -77,3 +77,19 @@ def test_decode_attention_kv_round_trip_is_lossless():
     flat, _, _ = zs.pad_kv_by_kv_head(k)
     kc = zs.compress_kv(k)
     assert torch.equal(zs.decompress(kc).view(torch.int16), flat.view(torch.int16))
+
+
+def test_kv_head_parallel_attention_single_rank_uses_the_kernel():
+    """KVHeadParallelDecodeAttention with its default backends (compress_kv +
+    decode_attention): one rank owns every head and matches the fp32 reference."""
+    from zipserv_asplos26_b200.tp import KVHeadParallelDecodeAttention
+    B, T, Hq, Hkv, D = 2, 300, 32, 8, 128
+    k, v = make_kv(B, T, Hkv, D, 21), make_kv(B, T, Hkv, D, 22)
+    q = torch.randn(B, Hq, D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(23)).to(
+        torch.bfloat16)
+    lens = torch.tensor([300, 129], dtype=torch.int32, device="cuda")
+    att = KVHeadParallelDecodeAttention(Hq, Hkv)
+    att.load_kv(att.shard_kv(k), att.shard_kv(v))
+    out = att(att.shard_q(q), lens)
+    ref = reference(q, k, v, lens, 1.0 / math.sqrt(D)).to(torch.bfloat16)
+    assert rel_l2(out, ref) <= TOL

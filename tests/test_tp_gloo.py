@@ -95,3 +95,58 @@ def test_tp_layer_shapes_single_rank():
     ys = lay.run(xs)
     for n, y in ys.items():
         assert y.shape == (3, small[n][0])
+
+
+def _ref_attention(q, k, v, seqlens, num_kv_heads):
+    """fp32 decode attention: q [B, Hq, D], k/v [B, T, Hkv, D] (dense, uncompressed)."""
+    B, Hq, D = q.shape
+    G = Hq // num_kv_heads
+    out = torch.empty(B, Hq, D)
+    for b in range(B):
+        t = int(seqlens[b])
+        for h in range(Hq):
+            kk, vv = k[b, :t, h // G].float(), v[b, :t, h // G].float()
+            p = torch.softmax(kk @ q[b, h].float() / D ** 0.5, 0)
+            out[b, h] = p @ vv
+    return out
+
+
+def _attn_worker(rank, world, port, q_out):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from zipserv_asplos26_b200.tp import KVHeadParallelDecodeAttention
+        torch.manual_seed(1)
+        B, T, Hq, Hkv, D = 2, 40, 8, 4, 16
+        q = torch.randn(B, Hq, D)
+        k, v = torch.randn(B, T, Hkv, D), torch.randn(B, T, Hkv, D)
+        seq = torch.tensor([40, 17])
+        ref = _ref_attention(q, k, v, seq, Hkv)
+        att = KVHeadParallelDecodeAttention(Hq, Hkv, compress_kv=_identity, attention=_ref_attention)
+        att.load_kv(att.shard_kv(k), att.shard_kv(v))
+        o = att(att.shard_q(q), seq)
+        gathered = [torch.empty_like(o) for _ in range(world)]
+        dist.all_gather(gathered, o)
+        q_out.put((rank, float((torch.cat(gathered, dim=1) - ref).abs().max()), att.q_heads))
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q_out.put((rank, repr(e), None))
+
+
+def test_kv_head_parallel_attention_matches_full():
+    """Sharding decode attention by KV head (with its query-head group) and
+    concatenating the ranks' heads reproduces full attention (gloo, 2 ranks)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_attn_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, err, heads in res:
+        assert not isinstance(err, str), err
+        assert err < 1e-5
+        assert heads == ((0, 4) if rank == 0 else (4, 8))

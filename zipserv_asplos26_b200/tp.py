@@ -116,3 +116,56 @@ class TPLayerGemms:
 
     def run(self, xs: dict):
         return {name: self.layers[name](xs[name]) for name in self.layers}
+
+
+def _compress_kv_backend(x):
+    from .attention import compress_kv
+    return compress_kv(x)
+
+
+def _decode_attention_backend(q, k, v, seqlens, num_kv_heads):
+    from .attention import decode_attention
+    return decode_attention(q, k, v, seqlens, num_kv_heads)
+
+
+class KVHeadParallelDecodeAttention:
+    """Decode attention sharded by KV head (no collective): rank r of `world`
+    owns KV heads [r Hkv/world, (r+1) Hkv/world) and the G = Hq/Hkv query heads
+    of each, so its output heads are contiguous and feed the row-parallel O
+    projection directly. Each rank compresses its own K/V heads (its own
+    exponent window), as a per-rank cache would be."""
+
+    def __init__(self, num_heads: int, num_kv_heads: int, group=None,
+                 compress_kv: Callable = _compress_kv_backend, attention: Callable = _decode_attention_backend):
+        rank, world = _rank_world(group)
+        if num_heads % num_kv_heads or num_kv_heads % world:
+            raise ValueError(f"{num_kv_heads} KV heads do not split over {world} ranks "
+                             f"(or {num_heads} heads are not a multiple of them)")
+        self.G = num_heads // num_kv_heads
+        self.kv_local = num_kv_heads // world
+        self.kv0 = rank * self.kv_local
+        self.compress_kv, self.attention = compress_kv, attention
+        self.k = self.v = None
+
+    @property
+    def q_heads(self):
+        """Query-head range [start, stop) this rank computes."""
+        return self.kv0 * self.G, (self.kv0 + self.kv_local) * self.G
+
+    def shard_kv(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's KV heads of a [B, T, Hkv, D] tensor."""
+        return x[:, :, self.kv0:self.kv0 + self.kv_local].contiguous()
+
+    def shard_q(self, q: torch.Tensor) -> torch.Tensor:
+        """This rank's query heads of a [B, Hq, D] tensor."""
+        a, b = self.q_heads
+        return q[:, a:b].contiguous()
+
+    def load_kv(self, k_local: torch.Tensor, v_local: torch.Tensor):
+        """Compress this rank's K and V ([B, T, Hkv/world, D])."""
+        self.k, self.v = self.compress_kv(k_local), self.compress_kv(v_local)
+
+    def __call__(self, q_local: torch.Tensor, seqlens: torch.Tensor) -> torch.Tensor:
+        if self.k is None:
+            raise RuntimeError("load_kv first")
+        return self.attention(q_local, self.k, self.v, seqlens, self.kv_local)
