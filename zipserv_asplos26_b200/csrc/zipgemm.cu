@@ -461,6 +461,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int seg_left = R.len0;
             bool first = true;
             for (int i = 0; i < R.n; ++i) {
+                if (i < 6) ZS_STAMP(42 + i);
                 if (first && racc.wrapped &&
                     !mbar_wait(&hd->acc_empty[racc.slot], racc.phase ^ 1u, p.err, abort_flag))
                     break;
@@ -476,8 +477,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     umma_bf16_ss(d, da + 4, db + 4, idesc, 1u);
                     umma_bf16_ss(d, da + 6, db + 6, idesc, 1u);
                 }
+                if (i < 6) ZS_STAMP(30 + i);
                 umma_commit(&hd->a_empty[sa]);
                 umma_commit(&hd->b_empty[sb]);
+                if (i < 6) ZS_STAMP(36 + i);
                 if (++sa == p.na) { sa = 0; pa ^= 1u; da = da0; } else { da += 1024; }
                 if (++sb == p.nb) { sb = 0; pb ^= 1u; db = db0; } else { db += bstep; }
                 first = false;
