@@ -1,7 +1,7 @@
 """Compressed-KV decode attention vs an fp32 torch reference on the original K/V.
 
 Decode is lossless, so the reference is exact attention on the uncompressed
-cache (SURVEY oracle for config 5), rounded to bf16 like any bf16-output kernel."""
+cache, rounded to bf16 like any bf16-output kernel."""
 import math
 
 import numpy as np
@@ -93,3 +93,20 @@ def test_kv_head_parallel_attention_single_rank_uses_the_kernel():
     out = att(att.shard_q(q), lens)
     ref = reference(q, k, v, lens, 1.0 / math.sqrt(D)).to(torch.bfloat16)
     assert rel_l2(out, ref) <= TOL
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(8, 8), (16, 8), (64, 8), (6, 2)])
+def test_decode_attention_query_group_sizes(Hq, Hkv):
+    """Query groups G = Hq / Hkv of 1, 2, 8 and 3 (the MMA tiles hold up to 8
+    query heads in their columns; unused columns must not leak into the output)."""
+    import zipserv_asplos26_b200 as zs
+    B, T, D = 2, 700, 128
+    k = make_kv(B, T, Hkv, D, seed=31 + Hq)
+    v = make_kv(B, T, Hkv, D, seed=32 + Hq)
+    q = torch.randn(B, Hq, D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(Hq)).to(
+        torch.bfloat16)
+    lens = torch.tensor([700, 333], dtype=torch.int32, device="cuda")
+    for splits in (1, 0):
+        out = zs.decode_attention(q, zs.compress_kv(k), zs.compress_kv(v), lens, Hkv, num_splits=splits)
+        ref = reference(q, k, v, lens.cpu(), 1.0 / math.sqrt(D)).to(torch.bfloat16)
+        assert rel_l2(out, ref) <= TOL, (Hq, Hkv, splits)

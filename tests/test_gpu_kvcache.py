@@ -46,7 +46,9 @@ def _rel(a, b):
 
 
 @pytest.mark.gpu
-def test_page_append_matches_matrix_encoder():
+def test_page_append_matches_matrix_encoder(oracle):
+    import numpy as np
+
     import zipserv_asplos26_b200 as zs
     gen = torch.Generator(device="cuda").manual_seed(11)
     Hkv = 2
@@ -72,6 +74,11 @@ def test_page_append_matches_matrix_encoder():
             for bi in range(3):
                 assert torch.equal(pool.b[bi][P * 128:(P + 1) * 128], getattr(c, f"bitmap{bi + 1}"))
             assert torch.equal(pool.mt_off[P * 16:(P + 1) * 16], c.tile_offsets_median)
+            # and the CPU oracle's encoding of the same page with the same window
+            e = oracle.encode(page.cpu().view(torch.int16).numpy().view(np.uint16), win.cpu().numpy())
+            assert np.array_equal(pool.sm[o[0]:o[4]].cpu().numpy(), e.sign_mantissa)
+            assert np.array_equal(pool.full[o[1]:o[5]].cpu().view(torch.int16).numpy().view(np.uint16), e.full)
+            assert np.array_equal(pool.b[0][P * 128:(P + 1) * 128].view(torch.int64).cpu().numpy().view(np.uint64), e.bitmap1)
 
 
 @pytest.mark.gpu
