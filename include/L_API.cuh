@@ -8,13 +8,12 @@
 // Behavioural notes (differences are strictly additive):
 //  * Inputs are validated on the host; bad shapes, null or misaligned pointers
 //    return cudaErrorInvalidValue instead of launching.
-//  * BF16TripleBitmap_MM_API splits K over all SMs itself (stream-K) and
-//    reduces split tiles inside the same kernel in a fixed order (deterministic
-//    fp32 sums, no bf16 rounding of partials). Reduction_Workspace is not used
-//    and may be nullptr; Split_K is accepted and ignored. The library keeps its
-//    own fp32 split-tile workspace per (device, stream), allocated on the first
-//    call on that stream (and grown for a larger shape): warm a stream up
-//    before capturing it into a CUDA graph.
+//  * BF16TripleBitmap_MM_API splits K itself: the K blocks of each 128-row
+//    output tile go to the CTAs of a thread-block cluster, whose fp32 partial
+//    tiles are summed in the same kernel through distributed shared memory in
+//    a fixed order (deterministic fp32 sums, no bf16 rounding of partials).
+//    Split_K is accepted and ignored; Reduction_Workspace is not used and may
+//    be nullptr. Like the reference, it allocates nothing.
 //  * All device work is ordered on `stream`; nothing synchronises the host.
 #pragma once
 #include <cuda.h>

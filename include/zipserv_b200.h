@@ -2,8 +2,8 @@
  *
  * Every function returns a cudaError_t value as int (0 = success). Pointers
  * named d_* are device pointers; `stream` is a cudaStream_t (NULL = legacy
- * default stream). Nothing here synchronises the host; only zs_zipgemm
- * allocates device memory (its split-tile workspace, once per stream). Each
+ * default stream). Nothing here synchronises the host or allocates device
+ * memory; buffers are the caller's. Each
  * entry point cites the reference interface it replaces
  * (paths inside the reference project).
  */
@@ -64,11 +64,13 @@ int zs_decompress(void* stream, const uint8_t* d_sm, const uint16_t* d_full, con
 
 /* ZipGEMM: d_c[n*M + m] = sum_k W[m][k] * d_x[n*K + k] (bf16 in/out, fp32 accumulate).
  * Replaces csrc/L_API.cu:119 BF16TripleBitmap_MM_API. The K split is chosen by
- * the library (stream-K over all SMs, split tiles reduced in-kernel in a fixed
- * order); split_k must be >= 1 and is otherwise ignored. The first call on a
- * stream allocates the library's fp32 split-tile workspace for that stream
- * (grown, with a stream synchronisation, when a larger shape arrives); make
- * that call outside CUDA-graph capture. d_x must be 16-byte aligned, d_c
+ * the library: the K blocks of each 128-row output tile are split over the CTAs
+ * of a thread-block cluster and the fp32 partial tiles are summed in-kernel
+ * through distributed shared memory, in a fixed order (deterministic results,
+ * no bf16 rounding of partials). split_k must be >= 1 and is otherwise
+ * ignored. No device memory is allocated and nothing is synchronised, so calls
+ * may be captured in CUDA graphs (the first call on a device sets kernel
+ * attributes; make it outside capture). d_x must be 16-byte aligned, d_c
  * 8-byte aligned. */
 int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const uint64_t* d_b1,
                const uint64_t* d_b2, const uint64_t* d_b3, const int* d_mt_off, const int* d_gt_off,

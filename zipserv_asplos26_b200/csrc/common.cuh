@@ -69,36 +69,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 }
 
 // One potentially blocking test of an mbarrier phase. The suspend-time hint
-// lets the hardware park the waiting thread (up to ~1 ms) until the phase
-// completes, so waiting warps do not spin and steal issue slots from the
-// decoders sharing the SM.
+// lets the hardware park the waiting thread until the phase completes (or
+// about 0.1 ms pass), so waiting warps take no issue slots from the warps
+// that share their scheduler.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
-#ifdef ZS_WAIT_HINT
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
         : "memory");
-#elif defined(ZS_TEST_WAIT)
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-#else
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-#endif
     return ok != 0;
 }
 
@@ -200,6 +182,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* m
             smem_u32(dst_smem)),
         "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
         : "memory");
+}
+
+// 8-byte asynchronous global -> shared copy (no register staging); complete with
+// cp_async_wait_all() in the issuing thread.
+__device__ __forceinline__ void cp_async8(void* dst_smem, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
