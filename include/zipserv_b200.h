@@ -109,8 +109,9 @@ int zs_decode_attention(void* stream, const uint16_t* d_q, const void* const* k_
  * the caller passes no workspace and nothing is allocated. Returns
  * cudaErrorInvalidValue when B * Hq * splits * (D + 2) * 4 bytes exceeds
  * zs_decode_attention_noalloc_max_workspace_bytes(). The first call on a
- * device looks up the array's address on that device; make that first call
- * outside any stream capture. All calls share the array: calls that overlap on
+ * device looks up the array's address on that device (and looks it up again
+ * after the device's context changes, e.g. after cudaDeviceReset); make that
+ * first call outside any stream capture. All calls share the array: calls that overlap on
  * the GPU (unordered streams) race; order them on one stream. */
 size_t zs_decode_attention_noalloc_max_workspace_bytes(void);
 int zs_decode_attention_noalloc(void* stream, const uint16_t* d_q, const void* const* k_ptrs, const int* k_meta,

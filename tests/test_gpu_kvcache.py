@@ -131,3 +131,29 @@ def test_pool_overflow_sets_error_bit():
     cache.prefill(0, k, v)
     torch.cuda.synchronize()
     assert cache.check_errors() & 2
+
+
+PAGED_LONG = [(32, 4129), (8, 16417), (1, 32801)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,T", PAGED_LONG, ids=[f"B{b}-T{t}" for b, t in PAGED_LONG])
+def test_paged_attention_long_contexts(B, T):
+    """The bench's paged cases (config-5 shapes, lengths T % 64 == 33 so each
+    sequence ends in a dense tail page) against attention on the original K/V."""
+    gen = torch.Generator(device="cuda").manual_seed(100 + B)
+    Hq, Hkv, D = 32, 8, 128
+    ks = [_kv(gen, T, Hkv) for _ in range(B)]
+    vs = [_kv(gen, T, Hkv) for _ in range(B)]
+    blocks = (T + 63) // 64
+    cache = PagedZipKVCache(num_blocks=B * blocks, max_batch=B, max_blocks_per_seq=blocks, num_kv_heads=Hkv,
+                            k_window=PagedZipKVCache.window_from(ks[0]), v_window=PagedZipKVCache.window_from(vs[0]),
+                            full_elems_per_page=2048, device=torch.device("cuda"))
+    for b in range(B):
+        cache.prefill(b, ks[b], vs[b])
+    q = torch.randn(B, Hq, D, device="cuda", generator=gen).to(torch.bfloat16)
+    ref = _ref_attention(q, ks, vs, 1.0 / math.sqrt(D))
+    for splits in (1, 0):
+        out = cache.attention(q, num_splits=splits)
+        torch.cuda.synchronize()
+        assert _rel(out, ref) <= TOL, (splits, _rel(out, ref))

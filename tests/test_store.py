@@ -114,3 +114,26 @@ def test_loaded_file_feeds_gpu_decoder_and_zipgemm(tmp_path):
     assert torch.equal(zs.decompress(d).view(torch.int16), w.view(torch.int16))
     x = torch.randn(64, 512, device="cuda").to(torch.bfloat16)
     assert torch.equal(zs.zipgemm(d, x).view(torch.int16), zs.zipgemm(c, x).view(torch.int16))
+
+
+@pytest.mark.parametrize("how", ["tile_too_long", "decreasing", "median_outside_tile", "median_nonzero_start"])
+def test_load_rejects_offsets_that_do_not_describe_the_streams(tmp_path, how):
+    """A file whose checksums are consistent but whose offsets are not (a buggy
+    writer, or a crafted file) is refused on load: decoders would otherwise be
+    sent past the staged streams."""
+    c = zs.compress_host(_weight(128, 128, 7))
+    gt = c.tile_offsets_global.clone()
+    mt = c.tile_offsets_median.clone()
+    if how == "tile_too_long":      # tile 0 claims tile 1's hf bytes too: more than max_hf allows
+        gt[2] = gt[4]
+    elif how == "decreasing":       # the fallback offsets of tile 1 go backwards
+        gt[3] = gt[5] + 8
+    elif how == "median_outside_tile":
+        mt[2] = int(gt[2]) + 16     # median tile 1 of tile 0 starts past the tile's end
+    else:
+        mt[0] = 16
+    c.tile_offsets_global, c.tile_offsets_median = gt, mt
+    path = tmp_path / "bad.zst"
+    store.save(c, path)             # the writer checksums whatever it is given
+    with pytest.raises(ZipServError):
+        store.load(path)

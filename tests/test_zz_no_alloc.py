@@ -79,13 +79,28 @@ def test_noalloc_attention_matches_regular_entry_point_twice():
 
 
 def test_noalloc_attention_rejects_workspace_beyond_its_array():
+    """A shape whose split-KV workspace exceeds the fixed array is refused with
+    an error status. Every input is real and valid for that shape (B=8, 8 query
+    and 8 KV heads, T=4096, 64 splits: 2.13 MB of workspace against the 2 MiB
+    array), so if the size check ever regressed the call would compute into
+    real buffers instead of touching unmapped addresses."""
+    import zipserv_asplos26_b200 as zs
     L = _lib()
     cap = L.zs_decode_attention_noalloc_max_workspace_bytes()
-    B, Hq, Hkv, D, splits = 64, 32, 8, 128, 64
-    assert B * Hq * splits * (D + 2) * 4 > cap
-    dummy = (C.c_void_p * 7)(*([1 << 20] * 7))
-    meta = (C.c_int * 5)(B * Hkv * 64 * splits, D, 4096, 0, 120)
-    rc = L.zs_decode_attention_noalloc(None, C.c_void_p(1 << 20), dummy, meta, dummy, meta, C.c_void_p(1 << 20),
-                                       B, Hq, Hkv, D, 64 * splits, 64 * splits, 0.1, splits, C.c_void_p(1 << 20),
-                                       None, None)
+    B, T, Hq, Hkv, D, splits = 8, 4096, 8, 8, 128, 64
+    assert L.zs_decode_attention_workspace_bytes(B, Hq, Hkv, splits) > cap
+    kc = zs.compress_kv(_kv(B, T, Hkv, D, 3))
+    vc = zs.compress_kv(_kv(B, T, Hkv, D, 4))
+    kp, km = _args(kc)
+    vp, vm = _args(vc)
+    q = torch.randn(B, Hq, D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5)).to(torch.bfloat16)
+    lens = torch.full((B,), T, dtype=torch.int32, device="cuda")
+    out = torch.full_like(q, 7.0)
+    used = C.c_int(-1)
+    rc = L.zs_decode_attention_noalloc(torch.cuda.current_stream().cuda_stream, q.data_ptr(), kp, km, vp, vm,
+                                       lens.data_ptr(), B, Hq, Hkv, D, T, T, 1.0 / math.sqrt(D), splits,
+                                       out.data_ptr(), C.byref(used), None)
+    torch.cuda.synchronize()
     assert rc != 0
+    assert used.value == -1                      # nothing was launched
+    assert bool((out == 7.0).all())              # the output was not written

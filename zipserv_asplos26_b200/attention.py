@@ -62,9 +62,9 @@ def decode_attention(q: torch.Tensor, k: Compressed, v: Compressed, cache_seqlen
         raise ValueError("K/V row count must be B * num_heads_k * T_pad and agree")
     t_pad = k.rows // (B * num_heads_k)
     seq = cache_seqlens.to(device=q3.device, dtype=torch.int32).contiguous()
-    if max_seqlen is None:
-        max_seqlen = int(seq.max().item()) if seq.numel() else 0
-    max_seqlen = min(max_seqlen, t_pad)
+    # the bound only sizes the split-KV grid; without one the padded length is
+    # used, so the call never reads cache_seqlens back to the host
+    max_seqlen = t_pad if max_seqlen is None else min(max_seqlen, t_pad)
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
     L = lib()
     splits = num_splits

@@ -641,20 +641,37 @@ static cudaError_t attention_core(cudaStream_t stream, const AttnCompressed& kc,
 constexpr size_t kNoAllocWsFloats = 512 * 1024;
 static __device__ __align__(256) float g_attn_noalloc_ws[kNoAllocWsFloats];
 
-// The array's device address for the current device, looked up once per
-// device (cudaGetSymbolAddress with that device current). The first call on a
-// device does this look-up; make that first call outside any stream capture.
+// The array's device address for the current device, looked up with that
+// device current (cudaGetSymbolAddress) the first time a context of the device
+// calls, and again whenever the device's current context has changed since
+// (after cudaDeviceReset the module is loaded anew and the array may move).
+// The first call on a device does this look-up; make that first call outside
+// any stream capture.
 static cudaError_t noalloc_ws_ptr(float** out) {
+    using CtxGetCurrent = CUresult (*)(CUcontext*);
+    static CtxGetCurrent get_ctx = nullptr;
     static float* ptrs[64] = {};
+    static CUcontext ctxs[64] = {};
     static std::mutex mu;
     int dev = 0;
     ZS_RETURN_IF_ERR(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> g(mu);
-    if (!ptrs[dev]) {
+    if (!get_ctx) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        ZS_RETURN_IF_ERR(cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+        get_ctx = reinterpret_cast<CtxGetCurrent>(fn);
+    }
+    CUcontext ctx = nullptr;
+    // the caller's device pointers were made in the current context, so one is current
+    if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx) return cudaErrorDeviceUninitialized;
+    if (!ptrs[dev] || ctxs[dev] != ctx) {
         void* ptr = nullptr;
         ZS_RETURN_IF_ERR(cudaGetSymbolAddress(&ptr, g_attn_noalloc_ws));
         ptrs[dev] = static_cast<float*>(ptr);
+        ctxs[dev] = ctx;
     }
     *out = ptrs[dev];
     return cudaSuccess;

@@ -226,8 +226,27 @@ extern "C" int zs_tcatbe_load(const char* path, ZsTcatbeInfo* info, uint8_t* sm,
         if (fread(dst[i], 1, bytes, fh.f) != bytes) return kErrIo;
         if (crc32(dst[i], bytes) != h.e[i].crc) return kErrInvalid;
     }
-    // The global offsets end at the stream totals.
+    // The offsets must describe streams the decoders can stage: the global
+    // offsets start at zero, never decrease, give each tile at most max_hf hf
+    // bytes and max_full fallback elements (padded to 16 bytes / 8 elements)
+    // and end at the stream totals; each tile's median-tile offsets start at
+    // zero, never decrease and stay inside the tile. (A file whose CRCs match
+    // but whose offsets do not would otherwise send the GPU decoders past the
+    // staged streams.)
     const uint64_t ngt = (uint64_t)in.rows * (uint64_t)in.cols / 4096;
+    const int64_t hcap = ((int64_t)in.max_hf + 15) / 16 * 16, fcap = ((int64_t)in.max_full + 7) / 8 * 8;
+    if (gt_off[0] != 0 || gt_off[1] != 0) return kErrInvalid;
+    for (uint64_t g = 0; g < ngt; ++g) {
+        const int64_t dh = (int64_t)gt_off[2 * g + 2] - gt_off[2 * g], df = (int64_t)gt_off[2 * g + 3] - gt_off[2 * g + 1];
+        if (dh < 0 || df < 0 || dh > hcap || df > fcap) return kErrInvalid;
+        if (mt_off) {
+            const int* m = mt_off + 8 * g;
+            if (m[0] != 0 || m[1] != 0) return kErrInvalid;
+            for (int w = 1; w < 4; ++w)
+                if (m[2 * w] < m[2 * w - 2] || m[2 * w + 1] < m[2 * w - 1] || m[2 * w] > dh || m[2 * w + 1] > df)
+                    return kErrInvalid;
+        }
+    }
     if ((int64_t)gt_off[2 * ngt] != in.total_hf || (int64_t)gt_off[2 * ngt + 1] != in.total_full) return kErrInvalid;
     *info = in;
     return 0;
