@@ -3,17 +3,22 @@ TCA-TBE compressed, X N=128 tokens ~ N(0, 1), SplitK=1, fp32 accumulate).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = one ZipGEMM launch over one weight matrix. Multi-GPU (torchrun):
-column-parallel weak scaling -- rank r holds output rows [4096 r, 4096 (r+1))
-of a (4096 N) x 4096 weight (its own compressed shard, seeded by r) and the
-same X; there is no data-path collective. The timed region is K CUDA-graph
-replayed steps bracketed by barrier + synchronize; time = max over ranks.
+One step = one config-2 GEMM. Multi-GPU (torchrun): row-parallel strong
+scaling, as a tensor-parallel O / down projection runs -- rank r holds columns
+[K r / N, K (r+1) / N) of W (its own compressed shard, seeded by r) and of X,
+and an NCCL all-reduce sums the partial Ys inside every step. The timed region
+is K CUDA-graph replayed steps bracketed by barrier + synchronize; time = max
+over ranks. Before the headline line, the config-4 Llama-70B layer at tp = N
+is printed (one line per token count).
 
 L2 policy: each rank rotates through enough distinct compressed weights that
 the rotating set exceeds the 126 MB L2, so every step streams its weight from
 HBM.
 
-`value` is algorithmic bytes per second: compressed W bytes + X (2KN) + Y (2MN).
+`value` is algorithmic bytes per second summed over the ranks: compressed W
+bytes + X (2KN) + Y (2MN) of each rank. The roofline is the ZipGEMM kernel's
+own (its launches alone, replayed in a graph); `dense_bf16_us` times cuBLAS on
+uncompressed weights at the same shape, as context.
 `e2e` repeats the step through the public API from pinned host memory (H2D of
 X + ZipGEMM + D2H of Y of every step inside the timed region, steps pipelined
 on three streams as a serving loop would run them). `cpu_baseline` times the CPU
@@ -167,7 +172,7 @@ def run_reference(args):
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded W ~ N(0,0.02), X ~ N(0,1))", "config": CONFIG,
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": desc + "; decoder = oracle port of the reference CPU decoder (its source "
@@ -449,25 +454,18 @@ def run_roundtrip(args):
                       "host_gpu_bytes_identical": bool(same), "round_trip_bit_exact": bool(exact)}), flush=True)
 
 
-def run_tp70b(args):
+def tp70b_lines(world, rank, dev, reps=20):
     """Config 4: one Llama-3.1-70B decoder layer's four weight GEMMs,
-    tensor-parallel over the torchrun ranks (QKV / gate_up column-parallel, O /
-    down row-parallel + NCCL all-reduce); per-layer device time = max over ranks.
-    Also times GPU compression of one layer's shards (x80 for the whole model)."""
+    tensor-parallel over the ranks (QKV / gate_up column-parallel, O / down
+    row-parallel + NCCL all-reduce), captured in one CUDA graph per N; per-layer
+    device time = max over ranks. Also times GPU compression of this rank's four
+    shards. Returns one dict per N (printed by rank 0)."""
     import torch
     import torch.distributed as dist
 
     import zipserv_asplos26_b200 as zs
     from zipserv_asplos26_b200.tp import LLAMA70B_SHAPES, TPLayerGemms
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
     layer = TPLayerGemms(LLAMA70B_SHAPES, seed=0, device=dev)
-    # GPU compression of this rank's four shards (weights generated outside the timed region)
     comp_ms, in_bytes = 0.0, 0
     for lin in layer.layers.values():
         w = (torch.randn(lin.out_features, lin.in_features, device=dev) * 0.02).to(torch.bfloat16)
@@ -481,36 +479,73 @@ def run_tp70b(args):
         comp_ms += e0.elapsed_time(e1)
         in_bytes += 2 * w.numel()
         del w
-    stream = torch.cuda.current_stream()
+    cb = sum(l.weight.compressed_bytes() for l in layer.layers.values())
+    stream = torch.cuda.Stream(device=dev)
+    out = []
     for N in (1, 16, 64):
         xs = {n: torch.randn(*shp, device=dev).to(torch.bfloat16) for n, shp in layer.input_shapes(N).items()}
-        for _ in range(3):
-            layer.run(xs)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = 20
-        a.record(stream)
-        for _ in range(reps):
-            layer.run(xs)
-        b.record(stream)
-        b.synchronize()
+        ys = {n: torch.empty(N, lin.out_features, dtype=torch.bfloat16, device=dev) for n, lin in layer.layers.items()}
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                for n, lin in layer.layers.items():
+                    lin(xs[n], out=ys[n])
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(reps):
+                    for n, lin in layer.layers.items():
+                        lin(xs[n], out=ys[n])
+            g.replay()
+            stream.synchronize()
+            if world > 1:
+                dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+            b.synchronize()
         t = torch.tensor([a.elapsed_time(b) * 1e3 / reps], device=dev)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        cb = sum(l.weight.compressed_bytes() for l in layer.layers.values())
-        if rank == 0:
-            print(json.dumps({"workload": "config4_tp70b_layer", "tp": world, "N": N, "layer_us": round(t.item(), 2),
-                              "per_rank_compressed_MB": round(cb / 1e6, 2),
-                              "per_rank_GBps": round(cb / t.item() / 1e3, 1),
-                              "compress_layer_ms": round(comp_ms, 2),
-                              "compress_GBps_bf16_in": round(in_bytes / comp_ms / 1e6, 1),
-                              "whole_model_compress_s_est": round(80 * comp_ms / 1e3, 2),
-                              "note": "4 projections per layer incl. 2 all-reduces; eager launches"}), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+        out.append({"workload": "config4_tp70b_layer", "tp": world, "N": N, "layer_us": round(t.item(), 2),
+                    "per_rank_compressed_MB": round(cb / 1e6, 2), "per_rank_GBps": round(cb / t.item() / 1e3, 1),
+                    "compress_layer_ms": round(comp_ms, 2),
+                    "compress_GBps_bf16_in": round(in_bytes / comp_ms / 1e6, 1),
+                    "note": "4 projections per layer incl. 2 NCCL all-reduces (bf16 sum), one CUDA graph of "
+                            f"{reps} layers, max over ranks"})
+        del g
+    return out
 
+
+def run_tp70b(args):
+    """--workload tp70b: the config-4 layer lines alone (under torchrun for tp > 1)."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    for line in tp70b_lines(world, rank, dev):
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    if world > 1:   # leave without tearing down the communicator (see main)
+        dist.barrier()
+        sys.stdout.flush()
+        os._exit(0)
+
+
+def dense_bf16_us(torch, dev, steps=40):
+    """torch.matmul (cuBLAS) at the config-2 shape on uncompressed bf16 weights
+    that rotate beyond L2: context for the ZipGEMM time, not a product path."""
+    sets = [(torch.randn(M_, K_, device=dev) * 0.02).to(torch.bfloat16) for _ in range(6)]
+    x = torch.randn(N_, K_, device=dev).to(torch.bfloat16)
+    y = torch.empty(N_, M_, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    return _graph_time_us(torch, [(lambda w=sets[i % 6]: torch.matmul(x, w.t(), out=y)) for i in range(steps)], stream)
 
 
 def main():
@@ -549,26 +584,66 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
     W = max(3, args.warmup)
     K = args.steps
+    if K_ % world or (K_ // world) % 64:
+        raise SystemExit(f"K={K_} does not split into multiples of 64 over {world} ranks")
+    Kr = K_ // world   # row-parallel: this rank's K slice of W and X
 
-    comps = make_weights(zs, torch, rank, 1, dev)
+    # One step = one config-2 GEMM Y = W X^T. With N ranks it runs row-parallel,
+    # as a tensor-parallel O / down projection would: rank r holds columns
+    # [r K/N, (r+1) K/N) of W (its own compressed shard) and of X, and the
+    # partial Ys are summed by an NCCL all-reduce inside the timed graph.
+    def make_shards(count, first=0):
+        out = []
+        for i in range(first, first + count):
+            g = torch.Generator(device=dev).manual_seed(1000 * rank + i)
+            w = (torch.randn(M_, Kr, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            out.append(zs.compress(w))
+            del w
+        return out
+
+    comps = make_shards(1)
     cb = comps[0].compressed_bytes()
     n_sets = max(2, -(-int(1.5 * L2_BYTES) // cb))
-    comps += make_weights(zs, torch, rank, n_sets - 1, dev, first=1)
-    x = torch.randn(N_, K_, generator=torch.Generator(device=dev).manual_seed(1), device=dev).to(torch.bfloat16)
+    comps += make_shards(n_sets - 1, first=1)
+    x_full = torch.randn(N_, K_, generator=torch.Generator(device=dev).manual_seed(1), device=dev).to(torch.bfloat16)
+    x = x_full[:, rank * Kr:(rank + 1) * Kr].contiguous()
     ys = [torch.empty(N_, M_, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    nbytes = cb + 2 * K_ * N_ + 2 * M_ * N_
+    nbytes = cb + 2 * Kr * N_ + 2 * M_ * N_          # this rank's algorithmic bytes per step
+    tb = torch.tensor([float(nbytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tb)
+    job_bytes = tb.item()                            # all ranks' algorithmic bytes per step
+
+    def step(i, xin, yout):
+        zs.zipgemm(comps[i % n_sets], xin, out=yout)
+        if world > 1:
+            dist.all_reduce(yout, op=dist.ReduceOp.SUM)
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
         for i in range(W):
-            zs.zipgemm(comps[i % n_sets], x, out=ys[i % 2])
+            step(i, x, ys[i % 2])
         stream.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             for i in range(K):
-                zs.zipgemm(comps[i % n_sets], x, out=ys[i % 2])
+                step(i, x, ys[i % 2])
         graph.replay()
         stream.synchronize()
+
+        # kernel-only time of the dominant kernel (the ZipGEMM launches alone)
+        kgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(kgraph, stream=stream):
+            for i in range(K):
+                zs.zipgemm(comps[i % n_sets], x, out=ys[i % 2])
+        kgraph.replay()
+        stream.synchronize()
+        ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ka.record(stream)
+        kgraph.replay()
+        kb.record(stream)
+        kb.synchronize()
+        gemm_ms = ka.elapsed_time(kb) / K
 
         sampler = ClockSampler(local)
         sampler.start()
@@ -591,40 +666,38 @@ def main():
         clocks = sampler.stop()
 
         # e2e through the public API from pinned host memory. Every step copies its
-        # X in (H2D), runs the GEMM and copies its Y out (D2H); steps are pipelined
-        # as a serving loop would run them: copies in, GEMMs and copies out on three
-        # streams with double-buffered device X and Y, so step i's D2H and step
-        # i+1's H2D overlap the GEMMs. Timed from the first H2D to the last D2H.
+        # X in (H2D), runs the GEMM (and the all-reduce) and copies its Y out (D2H);
+        # steps are pipelined as a serving loop would run them: copies in, GEMMs and
+        # copies out on three streams with NB device buffers each, so the copies of
+        # neighbouring steps overlap the GEMMs. Timed from the first H2D to the last D2H.
+        NB = 3
         xh = x.cpu().pin_memory()
-        yh = [torch.empty(N_, M_, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-        xd = [torch.empty_like(x) for _ in range(2)]
+        yh = [torch.empty(N_, M_, dtype=torch.bfloat16).pin_memory() for _ in range(NB)]
+        xd = [torch.empty_like(x) for _ in range(NB)]
+        yd = [torch.empty(N_, M_, dtype=torch.bfloat16, device=dev) for _ in range(NB)]
         s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
 
-        def e2e_steps(n, start=None, end=None):
+        def e2e_steps(n):
             ev_in = [torch.cuda.Event() for _ in range(n)]
             ev_c = [torch.cuda.Event() for _ in range(n)]
             ev_out = [torch.cuda.Event() for _ in range(n)]
-            if start is not None:
-                start.record(s_in)
             for i in range(n):
-                b = i % 2
+                b = i % NB
                 with torch.cuda.stream(s_in):
-                    if i >= 2:
-                        s_in.wait_event(ev_c[i - 2])          # GEMM i-2 has read xd[b]
+                    if i >= NB:
+                        s_in.wait_event(ev_c[i - NB])         # GEMM i-NB has read xd[b]
                     xd[b].copy_(xh, non_blocking=True)
                     ev_in[i].record(s_in)
                 with torch.cuda.stream(stream):
                     stream.wait_event(ev_in[i])
-                    if i >= 2:
-                        stream.wait_event(ev_out[i - 2])      # D2H i-2 has read ys[b]
-                    zs.zipgemm(comps[i % n_sets], xd[b], out=ys[b])
+                    if i >= NB:
+                        stream.wait_event(ev_out[i - NB])     # D2H i-NB has read yd[b]
+                    step(i, xd[b], yd[b])
                     ev_c[i].record(stream)
                 with torch.cuda.stream(s_out):
                     s_out.wait_event(ev_c[i])
-                    yh[b].copy_(ys[b], non_blocking=True)
+                    yh[b].copy_(yd[b], non_blocking=True)
                     ev_out[i].record(s_out)
-            if end is not None:
-                end.record(s_out)
 
         e2e_steps(W)
         torch.cuda.synchronize()
@@ -639,42 +712,56 @@ def main():
             stream.wait_stream(s_out)
         g2.replay()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         a, bb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         g2.replay()
         bb.record(stream)
         bb.synchronize()
         e2e_ms = a.elapsed_time(bb)
-    t = torch.tensor([ms_total, e2e_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms_total, e2e_ms, gemm_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total, e2e_ms = t.tolist()
+    ms_total, e2e_ms, gemm_ms = t.tolist()
     ms_step = ms_total / K
     peak, peak_kind = peaks()
-    achieved = nbytes / (ms_step / 1e3) / 1e9
+    achieved = nbytes / (gemm_ms / 1e3) / 1e9
     traffic = None
     if os.path.exists(PROFILE_TRAFFIC):
         with open(PROFILE_TRAFFIC) as f:
             traffic = json.load(f).get("dram_bytes_per_launch")
+    dense_us = dense_bf16_us(torch, dev) if world == 1 else None
+    # the config-4 layer at tp = N (printed before the headline, which stays last)
+    layer_lines = tp70b_lines(world, rank, dev)
     if rank == 0:
+        for line in layer_lines:
+            print(json.dumps(line), flush=True)
+        par = ("single GPU" if world == 1 else
+               f"row-parallel tp{world}: W and X split by K over the ranks (own compressed shard per rank), "
+               "NCCL all-reduce (bf16 sum) of Y in every step")
         line = {
-            "metric": METRIC, "value": world * nbytes * K / (ms_total / 1e3) / 1e9, "unit": "GB/s",
-            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step, "us_per_gemm": ms_step * 1e3,
-            "tflops": 2.0 * M_ * N_ * K_ / (ms_step / 1e3) / 1e12, "higher_is_better": True, "scaling": "weak",
+            "metric": METRIC, "value": job_bytes * K / (ms_total / 1e3) / 1e9, "unit": "GB/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
+            "zipgemm_us": gemm_ms * 1e3,
+            "tflops": 2.0 * M_ * N_ * K_ / (ms_step / 1e3) / 1e12, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded W ~ N(0,0.02) per rank and set, X ~ N(0,1))",
-            "config": dict(CONFIG, parallelism=f"column-parallel weak scaling, {world} shard(s)",
-                           rotating_sets=n_sets, compressed_bytes=cb, ratio=round(2 * M_ * K_ / cb, 4)),
+            "config": dict(CONFIG, parallelism=par, rotating_sets=n_sets, compressed_bytes_per_rank=cb,
+                           ratio=round(2 * M_ * Kr / cb, 4)),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
+                         "frac": achieved / peak, "traffic": traffic if world == 1 else None,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "algorithmic_bytes_per_launch": nbytes},
-            "e2e": {"value": world * nbytes * K / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
-                    "h2d_bytes_per_step": 2 * N_ * K_, "d2h_bytes_per_step": 2 * N_ * M_,
+                         "algorithmic_bytes_per_launch": nbytes,
+                         "kernel": "zs::zipgemm_kernel, CUDA-graph replay of the GEMMs alone, max over ranks"},
+            "e2e": {"value": job_bytes * K / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": 2 * N_ * Kr, "d2h_bytes_per_step": 2 * N_ * M_,
                     "ms_per_step": e2e_ms / K,
-                    "mode": "per step: H2D of X from pinned host, zipgemm, D2H of Y to pinned host; "
-                            "steps pipelined on three streams with double-buffered X and Y, "
-                            "the K steps' API calls captured in one CUDA graph and replayed"},
+                    "mode": "per step: H2D of X from pinned host, zipgemm (+ all-reduce), D2H of Y to pinned host; "
+                            f"steps pipelined on three streams with {NB} device buffers each, the K steps' API "
+                            "calls captured in one CUDA graph and replayed"},
+            "dense_bf16_us": dense_us,
+            "speedup_vs_dense_bf16": (dense_us / (gemm_ms * 1e3)) if dense_us else None,
             "gpu_launches": K,
             "clocks": clocks,
         }
@@ -683,8 +770,15 @@ def main():
             line["cpu_baseline"] = {"value": v / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
                                     "sample": desc, "ms_per_step": per * 1e3}
         print(json.dumps(line), flush=True)
+    # Graphs that captured NCCL collectives must be released before the process
+    # group goes away (destroying it under live graphs can block forever), and
+    # the ranks leave together without tearing the communicator down.
+    del graph, kgraph, g2
+    torch.cuda.synchronize()
     if world > 1:
-        dist.destroy_process_group()
+        dist.barrier()
+        sys.stdout.flush()
+        os._exit(0)
 
 
 if __name__ == "__main__":

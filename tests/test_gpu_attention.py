@@ -193,3 +193,28 @@ def test_decode_attention_matches_reference_staged_path(B, T):
     assert rel_l2(ours, exact) <= TOL
     assert rel_l2(staged, exact) <= STAGED_TOL
     assert rel_l2(ours, staged) <= STAGED_TOL
+
+
+SHARD_GRIDS = [(2, 1), (4, 1), (8, 1), (4, 2), (8, 4), (16, 2)]
+
+
+@pytest.mark.parametrize("world,batch_shards", SHARD_GRIDS, ids=[f"w{w}-b{b}" for w, b in SHARD_GRIDS])
+def test_sharded_decode_attention_kernel_per_rank(world, batch_shards):
+    """Every rank's shard of a KV-head x batch grid through the real kernel (one
+    GPU stands in for each rank in turn): each rank compresses its own K/V slice
+    and its outputs equal full attention on its sequences and heads."""
+    from zipserv_asplos26_b200.tp import KVHeadParallelDecodeAttention
+    B, T, Hq, Hkv, D = 8, 700, 32, 8, 128
+    k, v = make_kv(B, T, Hkv, D, 51), make_kv(B, T, Hkv, D, 52)
+    q = torch.randn(B, Hq, D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(53)).to(
+        torch.bfloat16)
+    lens = torch.tensor([700, 513, 64, 1, 699, 200, 333, 640], dtype=torch.int32, device="cuda")
+    ref = reference(q, k, v, lens.cpu(), 1.0 / math.sqrt(D)).to(torch.bfloat16)
+    for rank in range(world):
+        att = KVHeadParallelDecodeAttention(Hq, Hkv, batch_shards=batch_shards, rank=rank, world=world)
+        att.load_kv(att.shard_kv(k), att.shard_kv(v))
+        out = att(att.shard_q(q), lens)
+        a, b = att.q_heads
+        s0, s1 = att.batch_range(B)
+        assert out.shape == (s1 - s0, b - a, D)
+        assert rel_l2(out, ref[s0:s1, a:b]) <= TOL, (rank, rel_l2(out, ref[s0:s1, a:b]))

@@ -1,4 +1,4 @@
-"""Tensor-parallel sharding + all-reduce logic on CPU ranks (gloo, world size 2).
+"""Tensor-parallel sharding + all-reduce logic on CPU ranks (gloo, world sizes 2, 4, 8).
 
 The GEMM backend is injected (dense fp32 matmul on the decompressed shard is
 replaced by a plain matmul of the dense shard), so these tests check the
@@ -40,7 +40,7 @@ def _worker(rank, world, port, q):
         from zipserv_asplos26_b200.tp import (ColumnParallelZipLinear, RowParallelZipLinear, shard_cols,
                                               shard_rows)
         torch.manual_seed(0)
-        M, K, N = 256, 384, 5
+        M, K, N = 512, 1024, 5
         w = torch.randn(M, K)
         x = torch.randn(N, K)
         ref = x @ w.t()
@@ -59,7 +59,7 @@ def _worker(rank, world, port, q):
         q.put((rank, repr(e), None))
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_column_and_row_parallel_match_dense(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -111,42 +111,55 @@ def _ref_attention(q, k, v, seqlens, num_kv_heads):
     return out
 
 
-def _attn_worker(rank, world, port, q_out):
+def _attn_worker(rank, world, port, q_out, batch_shards=1):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world)
         from zipserv_asplos26_b200.tp import KVHeadParallelDecodeAttention
         torch.manual_seed(1)
-        B, T, Hq, Hkv, D = 2, 40, 8, 4, 16
+        B, T, Hq, Hkv, D = 4, 40, 16, 8, 16
         q = torch.randn(B, Hq, D)
         k, v = torch.randn(B, T, Hkv, D), torch.randn(B, T, Hkv, D)
-        seq = torch.tensor([40, 17])
+        seq = torch.tensor([40, 17, 1, 33])
         ref = _ref_attention(q, k, v, seq, Hkv)
-        att = KVHeadParallelDecodeAttention(Hq, Hkv, compress_kv=_identity, attention=_ref_attention)
+        att = KVHeadParallelDecodeAttention(Hq, Hkv, compress_kv=_identity, attention=_ref_attention,
+                                            batch_shards=batch_shards)
         att.load_kv(att.shard_kv(k), att.shard_kv(v))
-        o = att(att.shard_q(q), seq)
+        o = att.gather_batch(att(att.shard_q(q), seq))     # this rank's heads, every sequence
         gathered = [torch.empty_like(o) for _ in range(world)]
         dist.all_gather(gathered, o)
-        q_out.put((rank, float((torch.cat(gathered, dim=1) - ref).abs().max()), att.q_heads))
+        hs = att.head_shards
+        full = torch.cat(gathered[:hs], dim=1)             # the head groups of batch shard 0 cover all heads
+        q_out.put((rank, float((full - ref).abs().max()), att.q_heads, att.batch_range(B)))
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent
-        q_out.put((rank, repr(e), None))
+        q_out.put((rank, repr(e), None, None))
 
 
-def test_kv_head_parallel_attention_matches_full():
-    """Sharding decode attention by KV head (with its query-head group) and
-    concatenating the ranks' heads reproduces full attention (gloo, 2 ranks)."""
+ATTN_GRIDS = [(2, 1), (4, 1), (8, 1), (4, 2), (8, 4), (8, 2)]
+
+
+@pytest.mark.parametrize("world,batch_shards", ATTN_GRIDS, ids=[f"w{w}-b{b}" for w, b in ATTN_GRIDS])
+def test_kv_head_and_batch_parallel_attention_matches_full(world, batch_shards):
+    """Sharding decode attention by KV head (with its query-head group) and by
+    batch, then reassembling the ranks' outputs, reproduces full attention
+    (gloo ranks on CPU; the per-shard kernel runs in the GPU tests)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_attn_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_attn_worker, args=(r, world, port, q, batch_shards)) for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=180) for _ in range(2)]
+    res = [q.get(timeout=240) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
-    for rank, err, heads in res:
+    hs = world // batch_shards
+    G, per = 2, 8 // hs
+    for rank, err, heads, brange in res:
         assert not isinstance(err, str), err
         assert err < 1e-5
-        assert heads == ((0, 4) if rank == 0 else (4, 8))
+        h = rank % hs
+        assert heads == (h * per * G, (h + 1) * per * G)
+        nb = 4 // batch_shards
+        assert brange == ((rank // hs) * nb, (rank // hs + 1) * nb)

@@ -129,23 +129,62 @@ def _decode_attention_backend(q, k, v, seqlens, num_kv_heads):
 
 
 class KVHeadParallelDecodeAttention:
-    """Decode attention sharded by KV head (no collective): rank r of `world`
-    owns KV heads [r Hkv/world, (r+1) Hkv/world) and the G = Hq/Hkv query heads
-    of each, so its output heads are contiguous and feed the row-parallel O
-    projection directly. Each rank compresses its own K/V heads (its own
-    exponent window), as a per-rank cache would be."""
+    """Decode attention sharded by KV head and by batch (no collective in the
+    attention itself). The ranks form a grid of batch_shards x head_shards
+    (head_shards = world / batch_shards): rank r owns KV heads
+    [h Hkv/hs, (h+1) Hkv/hs) with h = r % hs, together with the G = Hq/Hkv query
+    heads of each, for the sequences [b B/bs, (b+1) B/bs) with b = r // hs. With
+    batch_shards = 1 a rank's output heads are contiguous for the whole batch and
+    feed the row-parallel O projection directly; batch sharding serves more
+    ranks than KV heads (or balances uneven sequence lengths), and
+    gather_batch() reassembles a head group's outputs over the batch. Each rank
+    compresses its own K/V slice (its own exponent window), as a per-rank cache
+    would be."""
 
     def __init__(self, num_heads: int, num_kv_heads: int, group=None,
-                 compress_kv: Callable = _compress_kv_backend, attention: Callable = _decode_attention_backend):
-        rank, world = _rank_world(group)
-        if num_heads % num_kv_heads or num_kv_heads % world:
-            raise ValueError(f"{num_kv_heads} KV heads do not split over {world} ranks "
+                 compress_kv: Callable = _compress_kv_backend, attention: Callable = _decode_attention_backend,
+                 batch_shards: int = 1, rank: Optional[int] = None, world: Optional[int] = None):
+        # rank / world default to the process group's; given explicitly, one
+        # process can stand in for any rank of a grid (tests, offline sharding)
+        grank, gworld = _rank_world(group)
+        rank = grank if rank is None else rank
+        world = gworld if world is None else world
+        if batch_shards < 1 or world % batch_shards:
+            raise ValueError(f"{batch_shards} batch shards do not divide {world} ranks")
+        hs = world // batch_shards
+        if num_heads % num_kv_heads or num_kv_heads % hs:
+            raise ValueError(f"{num_kv_heads} KV heads do not split over {hs} head shards "
                              f"(or {num_heads} heads are not a multiple of them)")
+        self.group, self.world = group, world
+        self.batch_shards, self.head_shards = batch_shards, hs
+        self.bshard, self.hshard = rank // hs, rank % hs
         self.G = num_heads // num_kv_heads
-        self.kv_local = num_kv_heads // world
-        self.kv0 = rank * self.kv_local
+        self.kv_local = num_kv_heads // hs
+        self.kv0 = self.hshard * self.kv_local
         self.compress_kv, self.attention = compress_kv, attention
         self.k = self.v = None
+
+    def batch_range(self, batch: int):
+        """Sequences [start, stop) this rank serves out of `batch`."""
+        if batch % self.batch_shards:
+            raise ValueError(f"batch {batch} does not split into {self.batch_shards} shards")
+        n = batch // self.batch_shards
+        return self.bshard * n, (self.bshard + 1) * n
+
+    def shard_batch(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's sequences of a batch-leading tensor (q, K/V or seqlens)."""
+        a, b = self.batch_range(x.shape[0])
+        return x[a:b].contiguous()
+
+    def gather_batch(self, out_local: torch.Tensor) -> torch.Tensor:
+        """All sequences of this rank's heads: all-gather over the ranks that
+        hold the same heads for the other batch shards (collective; identity
+        without batch sharding)."""
+        if self.batch_shards == 1:
+            return out_local
+        parts = [torch.empty_like(out_local) for _ in range(self.world)]
+        dist.all_gather(parts, out_local.contiguous(), group=self.group)
+        return torch.cat([parts[b * self.head_shards + self.hshard] for b in range(self.batch_shards)], dim=0)
 
     @property
     def q_heads(self):
@@ -153,19 +192,25 @@ class KVHeadParallelDecodeAttention:
         return self.kv0 * self.G, (self.kv0 + self.kv_local) * self.G
 
     def shard_kv(self, x: torch.Tensor) -> torch.Tensor:
-        """This rank's KV heads of a [B, T, Hkv, D] tensor."""
-        return x[:, :, self.kv0:self.kv0 + self.kv_local].contiguous()
+        """This rank's sequences and KV heads of a [B, T, Hkv, D] tensor."""
+        a, b = self.batch_range(x.shape[0])
+        return x[a:b, :, self.kv0:self.kv0 + self.kv_local].contiguous()
 
     def shard_q(self, q: torch.Tensor) -> torch.Tensor:
-        """This rank's query heads of a [B, Hq, D] tensor."""
+        """This rank's sequences and query heads of a [B, Hq, D] tensor."""
         a, b = self.q_heads
-        return q[:, a:b].contiguous()
+        s0, s1 = self.batch_range(q.shape[0])
+        return q[s0:s1, a:b].contiguous()
 
     def load_kv(self, k_local: torch.Tensor, v_local: torch.Tensor):
         """Compress this rank's K and V ([B, T, Hkv/world, D])."""
         self.k, self.v = self.compress_kv(k_local), self.compress_kv(v_local)
 
     def __call__(self, q_local: torch.Tensor, seqlens: torch.Tensor) -> torch.Tensor:
+        """q_local from shard_q; seqlens of the whole batch or of this rank's
+        sequences. Returns [B / batch_shards, Hq / head_shards, D]."""
         if self.k is None:
             raise RuntimeError("load_kv first")
+        if seqlens.shape[0] != q_local.shape[0]:
+            seqlens = self.shard_batch(seqlens)
         return self.attention(q_local, self.k, self.v, seqlens, self.kv_local)
