@@ -273,6 +273,10 @@ def run_llama8b(args):
             if i:
                 comps.append(zs.compress(w))
             dense.append(w)
+        if args.weight_offload:
+            _weight_offload_lines(torch, zs, name, M, K, comps[0], dense[0], stream, peak, kind)
+            del comps, dense
+            continue
         for N in (1, 8, 16, 32, 64, 128, 256):
             x = torch.randn(N, K, device=dev).to(torch.bfloat16)
             y = torch.empty(N, M, dtype=torch.bfloat16, device=dev)
@@ -290,6 +294,45 @@ def run_llama8b(args):
                               "peak": f"{peak} GB/s ({kind})", "split_k": "stream-K (SplitK argument is a hint)"}),
                   flush=True)
         del comps, dense
+
+
+def _weight_offload_lines(torch, zs, name, M, K, comp, dense, stream, peak, kind):
+    """Weight offload (reference kernel_benchmark/bench_zipserv_gemm_sweep.cu:608-661,
+    680-684): the weight lives in pinned host memory and every step copies it to
+    the device before the GEMM. Compressed: the TCA-TBE arrays cross PCIe, then
+    ZipGEMM; dense: the bf16 matrix crosses PCIe, then torch.matmul."""
+    from zipserv_asplos26_b200.codec import Compressed
+    fields = ("sign_mantissa", "compressed_full", "bitmap1", "bitmap2", "bitmap3", "tile_offsets_median",
+              "tile_offsets_global")
+    n_used = {"sign_mantissa": comp.total_hf, "compressed_full": comp.total_full}
+    host = {f: getattr(comp, f)[:n_used.get(f, getattr(comp, f).numel())].cpu().pin_memory() for f in fields}
+    devb = {f: torch.empty_like(getattr(comp, f)) for f in fields}
+    dc = Compressed(devb["sign_mantissa"], devb["compressed_full"], devb["bitmap1"], devb["bitmap2"], devb["bitmap3"],
+                    None, devb["tile_offsets_median"], devb["tile_offsets_global"], comp.rows, comp.cols,
+                    comp.max_high_freq_count, comp.max_full_count, comp.start_exp, comp.total_hf, comp.total_full)
+    wh = dense.cpu().pin_memory()
+    wd = torch.empty_like(dense)
+    h2d_comp = sum(t.numel() * t.element_size() for t in host.values())
+    for N in (1, 16, 64, 128):
+        x = torch.randn(N, K, device=dense.device).to(torch.bfloat16)
+        y = torch.empty(N, M, dtype=torch.bfloat16, device=dense.device)
+
+        def comp_step():
+            for f in fields:
+                devb[f][:host[f].numel()].copy_(host[f], non_blocking=True)
+            zs.zipgemm(dc, x, out=y)
+
+        def dense_step():
+            wd.copy_(wh, non_blocking=True)
+            torch.matmul(x, wd.t(), out=y)
+        tz = _graph_time_us(torch, [comp_step] * 10, stream)
+        td = _graph_time_us(torch, [dense_step] * 10, stream)
+        print(json.dumps({"workload": "config3_llama8b_weight_offload", "proj": name, "M": M, "K": K, "N": N,
+                          "compressed_step_us": round(tz, 2), "dense_step_us": round(td, 2),
+                          "speedup_vs_dense": round(td / tz, 3), "h2d_bytes_compressed": h2d_comp,
+                          "h2d_bytes_dense": 2 * M * K, "ratio": round(2 * M * K / h2d_comp, 4),
+                          "mode": "per step: H2D of the weight from pinned host memory, then the GEMM; "
+                                  "10 steps in one CUDA graph"}), flush=True)
 
 
 def run_attention(args):
@@ -332,8 +375,24 @@ def run_attention(args):
                                        for i in range(L)], stream)
             nbytes = cb + 2 * 2 * B * Hq * D
             dense = 2 * 2 * B * T * Hkv * D
+            # yardstick: stock flash-attn decode on the uncompressed cache (rotating
+            # beyond L2 where it fits), as the reference's dense baseline runs it
+            # (kernel_benchmark/bench_zipserv_decode_attention.py:610-649)
+            fa_us = None
+            try:
+                from flash_attn import flash_attn_with_kvcache
+                nd = max(1, min(8, -(-int(1.5 * L2_BYTES) // dense)))
+                dsets = [(kv(B, T), kv(B, T)) for _ in range(nd)]
+                q4 = q.view(B, 1, Hq, D)
+                fa_us = _graph_time_us(torch, [(lambda s=dsets[i % nd]: flash_attn_with_kvcache(
+                    q4, s[0], s[1], cache_seqlens=seq)) for i in range(L)], stream)
+                del dsets
+            except ImportError:
+                pass
             print(json.dumps({"workload": "config5_decode_attention", "B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "D": D,
                               "us": round(t, 2), "tok_per_s": round(B / (t * 1e-6), 1),
+                              "dense_flash_attn_us": round(fa_us, 2) if fa_us else None,
+                              "speedup_vs_dense_flash_attn": round(fa_us / t, 3) if fa_us else None,
                               "compressed_GBps": round(nbytes / t / 1e3, 1), "hbm_frac": round(nbytes / t / 1e3 / peak, 4),
                               "dense_equiv_GBps": round((dense + 4 * B * Hq * D) / t / 1e3, 1),
                               "kv_ratio": round(dense / cb, 4), "rotating_sets": nsets,
@@ -517,8 +576,48 @@ def tp70b_lines(world, rank, dev, reps=20):
     return out
 
 
+def compress80_line(world, rank, dev, layers=80):
+    """Whole-model GPU compression (config 4): all `layers` Llama-3.1-70B layers
+    of this rank's shards, each layer's four matrices generated on the device
+    (seeded per layer, outside the timed region) and compressed through the
+    public API; the compressions' device times are summed (max over ranks).
+    Reference: kernel_benchmark/bench_llama31_70b_compress.cu:923 ProcessTensor."""
+    import torch
+    import torch.distributed as dist
+
+    import zipserv_asplos26_b200 as zs
+    from zipserv_asplos26_b200.tp import LLAMA70B_SHAPES
+    total_ms, in_bytes, out_bytes = 0.0, 0, 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for layer in range(layers):
+        for i, (name, (M, K)) in enumerate(LLAMA70B_SHAPES.items()):
+            col = name in ("qkv", "gate_up")
+            m, k = (M // world, K) if col else (M, K // world)
+            g = torch.Generator(device=dev).manual_seed(layer * 64 + i * 8 + rank)
+            w = (torch.randn(m, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            torch.cuda.synchronize()
+            e0.record()
+            c = zs.compress(w)
+            e1.record()
+            e1.synchronize()
+            total_ms += e0.elapsed_time(e1)
+            in_bytes += 2 * w.numel()
+            out_bytes += c.compressed_bytes()
+            del w, c
+    t = torch.tensor([total_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"workload": "config4_whole_model_compression", "tp": world, "layers": layers,
+            "seconds": round(t.item() / 1e3, 4), "per_rank_bf16_GB": round(in_bytes / 1e9, 2),
+            "per_rank_compressed_GB": round(out_bytes / 1e9, 2), "ratio": round(in_bytes / out_bytes, 4),
+            "GBps_bf16_in": round(in_bytes / (t.item() / 1e3) / 1e9, 1),
+            "note": "each matrix compressed by zs.compress (window analysis + GPU encoder + size read-back); "
+                    "device time summed over the 320 matrices of the rank, max over ranks"}
+
+
 def run_tp70b(args):
-    """--workload tp70b: the config-4 layer lines alone (under torchrun for tp > 1)."""
+    """--workload tp70b: the config-4 layer lines (under torchrun for tp > 1) and
+    the whole-model compression line."""
     import torch
     import torch.distributed as dist
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -528,7 +627,7 @@ def run_tp70b(args):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
-    for line in tp70b_lines(world, rank, dev):
+    for line in tp70b_lines(world, rank, dev) + [compress80_line(world, rank, dev)]:
         if rank == 0:
             print(json.dumps(line), flush=True)
     torch.cuda.synchronize()
@@ -556,6 +655,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu", action="store_true", help="plain launches for ncu, no timing")
+    ap.add_argument("--weight-offload", action="store_true",
+                    help="with --workload llama8b: copy the weight H2D inside every timed step")
     ap.add_argument("--workload", default="config2",
                     choices=["config2", "llama8b", "attention", "roundtrip", "tp70b", "paged_kv"],
                     help="config2 = the headline line; the others print one JSON line per case")
@@ -645,10 +746,18 @@ def main():
         kb.synchronize()
         gemm_ms = ka.elapsed_time(kb) / K
 
+        # Load the GPU for about a second while the clock sampler runs. Every rank
+        # must replay the graph the same number of times (its collectives pair up
+        # across ranks), so the count comes from one timed replay, agreed by MAX.
+        t1 = time.perf_counter()
+        graph.replay()
+        stream.synchronize()
+        nsoak = torch.tensor([max(1, int(1.0 / max(time.perf_counter() - t1, 1e-4)))], device=dev)
+        if world > 1:
+            dist.all_reduce(nsoak, op=dist.ReduceOp.MAX)
         sampler = ClockSampler(local)
         sampler.start()
-        t_soak = time.perf_counter()
-        while time.perf_counter() - t_soak < 1.0:   # load the GPU while the sampler runs
+        for _ in range(int(nsoak.item())):
             graph.replay()
         stream.synchronize()
         if world > 1:

@@ -187,3 +187,18 @@ def test_gpu_zipgemm_deterministic(zs):
     y0 = zs.zipgemm(c, x)
     for _ in range(5):
         assert torch.equal(zs.zipgemm(c, x).view(torch.int16), y0.view(torch.int16))
+
+
+@pytest.mark.parametrize("counts", [[512] * 8, [455] * 8 + [456], [300, 700, 700, 300, 300, 700, 300, 300, 496],
+                                    [1] * 3 + [1000] * 2 + [1] * 6 + [2087]])
+@pytest.mark.parametrize("rule", ["host", "ext"])
+def test_gpu_window_rules_with_ties(zs, oracle, counts, rule):
+    """Histograms with equal counts at the seventh place, where the two rules'
+    tie-breaking (arg-max passes vs a replace-the-minimum slot list) decides
+    the window: the GPU picks what the reference-restating oracle picks."""
+    rng = np.random.default_rng(len(counts) + sum(counts))
+    exps = np.repeat(np.arange(100, 100 + len(counts)), counts)
+    rng.shuffle(exps)
+    a = ((exps.astype(np.uint16) << 7) | rng.integers(0, 128, exps.size).astype(np.uint16)).reshape(64, 64)
+    top = zs.analyze_exponents(to_dev(a), rule).cpu().numpy()
+    assert np.array_equal(top, oracle.analyze(a, rule))

@@ -2,14 +2,17 @@
 // Replaces csrc/L_Kernel.cuh:1110 BF16TripleBitmap_Decompress_Kernel and
 // csrc/L_API.cu:234 BF16TripleBitmap_Decompress_API.
 //
-// One CTA (8 warps) per group of four 64x64 global tiles. Thread 0 pulls each
-// GT's five streams into shared memory with 1-D bulk copies (the GT's hf and
-// fallback streams are contiguous and 16-byte aligned thanks to the format's
-// per-GT padding); two warps per GT then decode 32 rows each with the
-// branch-free row decoder into a bank-swizzled 64x64 tile, and the CTA writes
-// the tiles out with 16-byte coalesced stores (8 threads per 128-byte row).
-// The decoder is latency bound per warp, so the CTA is kept small enough for
-// several to share an SM.
+// One CTA (8 warps) per run of four consecutive 64x64 global tiles (GTs).
+// Consecutive GTs are contiguous in every array of the format (bitmaps and
+// median offsets are indexed by GT, the streams by the global prefix), so six
+// lanes of warp 0 pull the whole run with six 1-D bulk copies (bitmaps 1-3,
+// median offsets, sign/mantissa and fallback streams; the issue cost of a bulk
+// copy grows with the copies per instruction, not with their size). Two warps
+// per GT then decode a pair of median tiles each with the table-free row
+// decoder into a swizzled 64x64 tile, and the CTA writes the tiles out with
+// 16-byte coalesced stores (8 threads per 128-byte row). About 55 KB of shared
+// memory per CTA lets four CTAs share an SM, so copies, decoding and stores of
+// different CTAs overlap.
 #include "common.cuh"
 #include "tile_decode.cuh"
 #include "zs_internal.h"
@@ -20,32 +23,20 @@ constexpr int kDecompGTs = 4;                     // global tiles per CTA
 constexpr int kDecompThreads = 64 * kDecompGTs;   // two warps per GT
 
 struct DecompSmemLayout {
-    uint32_t lut, bar, gt_base, gt_stride, bm, mt, hfs, fulls, tile, total;
+    uint32_t bar, bm, mt, hfs, fulls, tiles, total;
+    uint32_t hf_cap, full_cap;   // bytes / elements the run's streams may hold
     __host__ __device__ DecompSmemLayout(int max_hf, int max_full) {
-        lut = 0;                          // replicated spread table
-        bar = 4 * kLutWords;              // mbarrier
-        gt_base = bar + 16;
-        bm = 0;                           // 3 x 512 B
-        mt = 1536;                        // 32 B
-        hfs = 1568;                       // hf slot
-        fulls = hfs + hf_slot_bytes(max_hf);
-        tile = round_up_u32(fulls + full_slot_bytes(max_full), 16);
-        gt_stride = round_up_u32(tile + 8192, 16);
-        total = gt_base + kDecompGTs * gt_stride;
+        hf_cap = round_up_u32((uint32_t)max_hf, 16) * kDecompGTs;
+        full_cap = round_up_u32((uint32_t)max_full, 8) * kDecompGTs;
+        bar = 0;                                   // mbarrier
+        bm = 128;                                  // [3 planes][4 GTs][512 B]
+        mt = bm + 3 * 512 * kDecompGTs;            // [4 GTs][32 B]
+        hfs = mt + 32 * kDecompGTs;                // hf streams of the run (+16 B read slack)
+        fulls = hfs + hf_cap + 16;                 // fallback streams of the run (+16 B)
+        tiles = round_up_u32(fulls + 2 * full_cap + 16, 1024);   // [4 GTs][64 rows][128 B], swizzled
+        total = tiles + 8192 * kDecompGTs;
     }
 };
-
-__device__ __forceinline__ void issue_gt_copies(uint8_t* base, const DecompSmemLayout& L, long long gt,
-                                                const GtCopy& c, const uint8_t* sm, const uint16_t* full,
-                                                const uint64_t* b1, const uint64_t* b2, const uint64_t* b3,
-                                                const int* mt_off, uint64_t* bar) {
-    bulk_g2s(base + L.bm, b1 + gt * 64, 512, bar);
-    bulk_g2s(base + L.bm + 512, b2 + gt * 64, 512, bar);
-    bulk_g2s(base + L.bm + 1024, b3 + gt * 64, 512, bar);
-    bulk_g2s(base + L.mt, mt_off + gt * 8, 32, bar);
-    if (c.hb) bulk_g2s(base + L.hfs, sm + c.h0, c.hb, bar);
-    if (c.fb) bulk_g2s(base + L.fulls, full + c.f0, c.fb, bar);
-}
 
 __global__ void __launch_bounds__(kDecompThreads) decompress_kernel(const uint8_t* __restrict__ sm,
                                                          const uint16_t* __restrict__ full,
@@ -58,61 +49,80 @@ __global__ void __launch_bounds__(kDecompThreads) decompress_kernel(const uint8_
                                                          unsigned* err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const DecompSmemLayout L(max_hf, max_full);
-    uint32_t* lut = reinterpret_cast<uint32_t*>(smem + L.lut);
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
     __shared__ int abort_flag;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gtk = K / kGT;
     const long long ngt = (long long)(M / kGT) * gtk;
     const long long gt0 = (long long)kDecompGTs * blockIdx.x;
     const int nsub = (int)min((long long)kDecompGTs, ngt - gt0);
+    const int2* go = reinterpret_cast<const int2*>(gt_off);
 
-    fill_spread_table(lut, tid, kDecompThreads);
     if (tid == 0) {
         abort_flag = 0;
         mbar_init(bar, 1);
         fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0) {
-        GtCopy c[kDecompGTs];
-        uint32_t total = 0;
-        for (int s = 0; s < nsub; ++s) {
-            c[s] = gt_copy_range(gt_off, gt0 + s, max_hf, max_full, err);
-            total += 3 * 512 + 32 + c[s].hb + c[s].fb;
+    if (warp == 0) {
+        // lanes 0-2: bitmap planes, 3: median offsets, 4: hf streams, 5: fallback streams of the run
+        const int2 f = go[gt0], e = go[gt0 + nsub];
+        uint32_t bytes = 0, dst = 0;
+        const void* src = nullptr;
+        if (lane < 3) {
+            bytes = 512u * (uint32_t)nsub;
+            src = (lane == 0 ? b1 : lane == 1 ? b2 : b3) + gt0 * 64;
+            dst = L.bm + 512u * kDecompGTs * (uint32_t)lane;
+        } else if (lane == 3) {
+            bytes = 32u * (uint32_t)nsub;
+            src = mt_off + gt0 * 8;
+            dst = L.mt;
+        } else if (lane < 6) {
+            const bool hf = lane == 4;
+            const int beg = hf ? f.x : f.y, end = hf ? e.x : e.y;
+            const uint32_t cap = hf ? L.hf_cap : 2u * L.full_cap;
+            const int al = hf ? 16 : 8;
+            uint32_t b = end > beg ? (uint32_t)(end - beg) * (hf ? 1u : 2u) : 0u;
+            int b0 = beg;
+            if (b > cap || (b & 15u) || (b0 & (al - 1)) || b0 < 0) {   // corrupt offsets: clamp, report
+                if (err) atomicOr(err, kErrStreamOverflow);
+                b = min(b, cap) & ~15u;
+                b0 = max(b0, 0) & ~(al - 1);
+            }
+            bytes = b;
+            src = hf ? (const void*)(sm + b0) : (const void*)(full + b0);
+            dst = hf ? L.hfs : L.fulls;
         }
-        // expect_tx is posted before any copy so the phase cannot complete early.
-        mbar_arrive_expect_tx(bar, total);
-        for (int s = 0; s < nsub; ++s)
-            issue_gt_copies(smem + L.gt_base + s * L.gt_stride, L, gt0 + s, c[s], sm, full, b1, b2, b3, mt_off,
-                            bar);
+        const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, bytes);
+        if (lane == 0) mbar_arrive_expect_tx(bar, total);   // posted before any copy lands
+        __syncwarp();
+        if (bytes) bulk_g2s(smem + dst, src, bytes, bar);
     }
     const bool ok = mbar_wait(bar, 0, err, &abort_flag);
-    const int warp = tid >> 5;
     const int sub = warp >> 1;
-    const DecodeTables tabs = make_decode_tables(start_exp);
     if (ok && sub < nsub) {
-        const uint32_t base = launder(smem_u32(smem + L.gt_base + sub * L.gt_stride));
+        const DecodeTables tabs = make_decode_tables(start_exp);
+        const int2 f0 = go[gt0], fs = go[gt0 + sub];   // stream starts of the run and of this GT
+        const uint32_t h0 = min((uint32_t)max(fs.x - f0.x, 0), L.hf_cap);
+        const uint32_t q0 = min((uint32_t)max(fs.y - f0.y, 0), L.full_cap);
+        const uint32_t base = launder(smem_u32(smem));
         GtView g;
-        g.bm = base + L.bm;
-        g.bstride = 512;
-        g.mt = base + L.mt;
-        g.sm = base + L.hfs;
-        g.full = base + L.fulls;
-        g.hf_cap = hf_slot_bytes(max_hf) - 16;
-        g.full_cap = full_slot_bytes(max_full) / 2 - 8;
-        const uint32_t lut_lane = launder(smem_u32(lut)) + 4u * (uint32_t)(tid & 31);
-        if (warp & 1)
-            decode_gt_rows<true, 8>(g, lut_lane, tabs, base + L.tile, 0);
-        else
-            decode_gt_rows<false, 8>(g, lut_lane, tabs, base + L.tile, 0);
+        g.bm = base + L.bm + 512u * (uint32_t)sub;
+        g.bstride = 512u * kDecompGTs;
+        g.mt = base + L.mt + 32u * (uint32_t)sub;
+        g.sm = base + L.hfs + h0;
+        g.full = base + L.fulls + 2u * q0;
+        g.hf_cap = L.hf_cap - h0;
+        g.full_cap = L.full_cap - q0;
+        const int w0 = 2 * (warp & 1);   // median tiles w0, w0 + 1 (rows 16 w0 .. 16 w0 + 31)
+        decode_mt2_to_tile(g, tabs, w0, base + L.tiles + 8192u * (uint32_t)sub + 128u * (uint32_t)(16 * w0));
     }
     __syncthreads();
     if (!ok) return;
     for (int idx = tid; idx < nsub * 512; idx += kDecompThreads) {
         const int s = idx >> 9, row = (idx >> 3) & 63, c = idx & 7;
         const long long gt = gt0 + s;
-        const uint8_t* tile = smem + L.gt_base + s * L.gt_stride + L.tile;
+        const uint8_t* tile = smem + L.tiles + s * 8192;
         const uint4 v = *reinterpret_cast<const uint4*>(tile + row * 128 + ((c ^ (row & 7)) << 4));
         const size_t grow = (size_t)(gt / gtk) * kGT + row;
         const size_t gcol = (size_t)(gt % gtk) * kGT + c * 8;
@@ -129,7 +139,7 @@ cudaError_t launch_decompress(cudaStream_t stream, const uint8_t* sm, const uint
     if (!b1 || !b2 || !b3 || !mt_off || !gt_off || !out) return cudaErrorInvalidValue;
     if ((max_hf > 0 && !sm) || (max_full > 0 && !full)) return cudaErrorInvalidValue;
     if (!aligned16(sm) || !aligned16(full) || !aligned16(b1) || !aligned16(b2) || !aligned16(b3) ||
-        !aligned16(mt_off) || !aligned16(out))
+        !aligned16(mt_off) || !aligned16(out) || (reinterpret_cast<uintptr_t>(gt_off) & 7u))
         return cudaErrorInvalidValue;
     const long long ngt = (long long)(M / 64) * (K / 64);
     const DecompSmemLayout L(max_hf, max_full);

@@ -6,7 +6,7 @@
 // Pipeline (all stream-ordered, no host synchronisation, no spin-waits):
 //   analyze_kernel  exponent histogram (warp-private shared bins, 16-byte
 //                   loads); the last CTA to finish (atomic ticket) picks the
-//                   7-exponent window.
+//                   7-exponent window, its 256 threads ranking one exponent each.
 //   count_kernel    one CTA per 64x64 GT: padded hf / fallback counts.
 //   scan_kernel     one CTA: exclusive prefix of the per-GT counts
 //                   (TileOffsets_Global), maxima and totals.
@@ -21,30 +21,12 @@
 namespace zs {
 
 // ------------------------------ window selection ---------------------------
-__device__ void select_window(const unsigned long long* cnt, int rule, int* top) {
-    int picks[7];
-    int np = 0;
-    if (rule == kRuleHost) {
-        bool used[256];
-        for (int e = 0; e < 256; ++e) used[e] = false;
-        for (int t = 0; t < 7; ++t) {
-            int best = -1;
-            unsigned long long bc = 0;
-            for (int e = 0; e < 256; ++e)
-                if (!used[e] && cnt[e] > bc) { bc = cnt[e]; best = e; }
-            if (best >= 0) { picks[np++] = best; used[best] = true; }
-        }
-    } else {
-        int te[7];
-        long long tc[7];
-        for (int i = 0; i < 7; ++i) { te[i] = -1; tc[i] = -1; }
-        for (int e = 0; e < 256; ++e) {
-            int mi = 0;
-            for (int i = 1; i < 7; ++i) if (tc[i] < tc[mi]) mi = i;
-            if ((long long)cnt[e] > tc[mi]) { tc[mi] = (long long)cnt[e]; te[mi] = e; }
-        }
-        for (int i = 0; i < 7; ++i) if (te[i] >= 0) picks[np++] = te[i];
-    }
+// Window rule from the 7 picked exponents (sorted here): the first start in the
+// picks whose 7 consecutive exponents all occur, else the longest run of
+// consecutive picks (kernel_benchmark/utils.h:240-272; the extension rule of
+// zipserv_decode_attention_ext.cu:100-133 also clamps the start to [0, 248]).
+// cnt: the 256-bin histogram. The host rule pads missing picks with 127 - np.
+__device__ void window_from_picks(const unsigned long long* cnt, int* picks, int np, int rule, int* top) {
     while (np < 7) { picks[np] = 127 - np; ++np; }
     for (int i = 1; i < 7; ++i) {
         int v = picks[i], j = i - 1;
@@ -71,6 +53,59 @@ __device__ void select_window(const unsigned long long* cnt, int rule, int* top)
     }
     if (rule == kRuleExt) best_start = min(max(best_start, 0), 248);
     for (int i = 0; i < 7; ++i) top[i] = best_start + i;
+}
+
+// The 7 picks of both rules. Host rule (utils.h:189-239): 7 arg-max passes
+// with a strict '>' from zero, i.e. the first 7 exponents in the order (count
+// descending, exponent ascending) among those that occur; every one of the 256
+// threads ranks its own exponent in that order at once. Extension rule
+// (zipserv_decode_attention_ext.cu:65-99): a replace-the-minimum top 7 seeded
+// with -1 that replaces the lowest-index slot holding the minimum on a strictly
+// larger count. Which tied minimum it drops depends on the slot history, so it
+// is run as written, by one thread, with the seven slots in registers.
+// cnt: the histogram in shared memory; all kAnalyzeThreads (= 256) threads call.
+__device__ void select_window_parallel(const unsigned long long* cnt, int rule, int* top, unsigned* masks) {
+    const int e = threadIdx.x;
+    if (rule == kRuleHost) {
+        const unsigned long long c = cnt[e];
+        int rank = 0;
+        for (int f = 0; f < 256; ++f) {
+            const unsigned long long d = cnt[f];
+            rank += (d > c || (d == c && f < e)) ? 1 : 0;
+        }
+        const unsigned m = __ballot_sync(0xFFFFFFFFu, rank < 7 && c > 0);
+        if ((e & 31) == 0) masks[e >> 5] = m;
+    }
+    __syncthreads();
+    if (e == 0) {
+        int picks[7], np = 0;
+        if (rule == kRuleHost) {
+            for (int w = 0; w < 8; ++w)
+                for (unsigned mm = masks[w]; mm && np < 7; mm &= mm - 1) picks[np++] = 32 * w + __ffs(mm) - 1;
+        } else {
+            int te[7];
+            long long tc[7];
+#pragma unroll
+            for (int i = 0; i < 7; ++i) { te[i] = -1; tc[i] = -1; }
+            for (int f = 0; f < 256; ++f) {
+                const long long c = (long long)cnt[f];
+                int mi = 0;
+                long long mv = tc[0];
+#pragma unroll
+                for (int i = 1; i < 7; ++i)
+                    if (tc[i] < mv) { mv = tc[i]; mi = i; }
+                if (c > mv) {
+#pragma unroll
+                    for (int i = 0; i < 7; ++i)
+                        if (i == mi) { tc[i] = c; te[i] = f; }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 7; ++i)
+                if (te[i] >= 0) picks[np++] = te[i];
+        }
+        window_from_picks(cnt, picks, np, rule, top);
+    }
 }
 
 constexpr int kAnalyzeThreads = 256;
@@ -108,11 +143,13 @@ __global__ void __launch_bounds__(kAnalyzeThreads) analyze_kernel(const uint16_t
     __syncthreads();
     if (tid == 0) last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
     __syncthreads();
-    if (last && tid == 0) {
+    if (last) {   // CTA-uniform: the last CTA to finish picks the window from the full histogram
+        __shared__ unsigned long long hist[256];
+        __shared__ unsigned masks[8];
         __threadfence();
-        unsigned long long c[256];
-        for (int e = 0; e < 256; ++e) c[e] = *((volatile unsigned long long*)counts + e);
-        select_window(c, rule, top);
+        hist[tid] = *((volatile unsigned long long*)counts + tid);
+        __syncthreads();
+        select_window_parallel(hist, rule, top, masks);
     }
 }
 
