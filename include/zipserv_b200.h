@@ -77,6 +77,12 @@ int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const 
                int max_hf, int max_full, int start_exp, const uint16_t* d_x, uint16_t* d_c, int M, int N,
                int K, int split_k, unsigned* d_err);
 
+/* The split-KV factor zs_decode_attention picks when num_splits <= 0, for B
+ * sequences of Hkv KV heads and up to max_seqlen tokens (a grid that fills the
+ * SMs in few, full waves). New relative to the reference, whose FlashAttention
+ * picks its own splits internally (FA flash_api.cpp num_splits_heuristic). */
+int zs_decode_attention_default_splits(int B, int Hkv, int max_seqlen);
+
 /* Workspace (device bytes) needed by zs_decode_attention for a split count
  * (0 when num_splits <= 1). */
 size_t zs_decode_attention_workspace_bytes(int B, int Hq, int Hkv, int num_splits);

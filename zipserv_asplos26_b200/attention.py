@@ -67,10 +67,7 @@ def decode_attention(q: torch.Tensor, k: Compressed, v: Compressed, cache_seqlen
     max_seqlen = t_pad if max_seqlen is None else min(max_seqlen, t_pad)
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
     L = lib()
-    splits = num_splits
-    if splits <= 0:
-        sms = torch.cuda.get_device_properties(q3.device).multi_processor_count
-        splits = max(1, min((2 * sms + B * num_heads_k - 1) // (B * num_heads_k), (max_seqlen + 63) // 64))
+    splits = num_splits if num_splits > 0 else L.zs_decode_attention_default_splits(B, num_heads_k, max_seqlen)
     ws_bytes = L.zs_decode_attention_workspace_bytes(B, Hq, num_heads_k, splits)
     ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device=q3.device)
     if out is None:

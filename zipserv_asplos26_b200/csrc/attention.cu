@@ -520,12 +520,27 @@ size_t attn_workspace_bytes(int B, int Hq, int Hkv, int num_splits) {
     return (size_t)B * Hq * num_splits * (kAttnD + 2) * sizeof(float);
 }
 
-static int attn_default_splits(int B, int Hkv, int max_pages) {
+// Split-KV factor for (B, Hkv) sequences of up to max_pages pages. One CTA per
+// (sequence, KV head, split) fills an SM (its page rings take most of the
+// shared memory), so the grid runs in ceil(B Hkv S / #SMs) waves of
+// ceil(max_pages / S) pages each; S minimises waves x (pages per CTA + 2), the
+// 2 standing for a CTA's set-up and its share of the combine. (A count that
+// only targeted about two CTAs per SM left 320 CTAs = 2.2 waves at B = 8,
+// T = 32768: a last wave 16% full.)
+int attn_default_splits(int B, int Hkv, int max_pages) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int s = std::max(1, (2 * sms + B * Hkv - 1) / (B * Hkv));
-    return std::min(s, std::max(1, max_pages));
+    const long long pairs = (long long)std::max(1, B) * std::max(1, Hkv);
+    const int P = std::max(1, max_pages);
+    int best = 1;
+    long long best_cost = -1;
+    for (int S = 1; S <= P; ++S) {
+        const long long waves = (pairs * S + sms - 1) / sms;
+        const long long cost = waves * ((P + S - 1) / S + 2);
+        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = S; }
+    }
+    return best;
 }
 
 static cudaError_t attention_core(cudaStream_t stream, const AttnCompressed& kc, const AttnCompressed& vc,

@@ -82,6 +82,11 @@ extern "C" int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_f
                               max_full, start_exp, d_x, d_c, M, N, K, split_k, d_err);
 }
 
+extern "C" int zs_decode_attention_default_splits(int B, int Hkv, int max_seqlen) {
+    if (B <= 0 || Hkv <= 0 || max_seqlen < 0) return 1;
+    return zs::attn_default_splits(B, Hkv, (max_seqlen + 63) / 64);
+}
+
 extern "C" size_t zs_decode_attention_workspace_bytes(int B, int Hq, int Hkv, int num_splits) {
     return zs::attn_workspace_bytes(B, Hq, Hkv, num_splits);
 }

@@ -53,6 +53,7 @@ struct AttnCompressed {
 };
 
 size_t attn_workspace_bytes(int B, int Hq, int Hkv, int num_splits);
+int attn_default_splits(int B, int Hkv, int max_pages);
 
 cudaError_t launch_attention(cudaStream_t s, const AttnCompressed& k, const AttnCompressed& v, const uint16_t* q,
                              const int* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int T_pad,

@@ -46,6 +46,7 @@ _SIGS = {
     "zs_decode_attention_paged": ([_P, _P, C.POINTER(ZsKvPool), C.POINTER(ZsKvPool), _P, C.c_int, _P, _P, _P]
                                   + [C.c_int] * 5 + [C.c_float, C.c_int, _P, C.c_size_t, _P, _P, _P], C.c_int),
     "zs_decode_attention_workspace_bytes": ([C.c_int] * 4, C.c_size_t),
+    "zs_decode_attention_default_splits": ([C.c_int] * 3, C.c_int),
 }
 
 
@@ -217,10 +218,7 @@ class PagedZipKVCache:
         scale = softmax_scale if softmax_scale is not None else D_HEAD ** -0.5
         max_len = max(self.lengths[:B]) if B else 0
         pages = (max_len + 63) // 64
-        splits = num_splits
-        if splits <= 0:
-            sms = torch.cuda.get_device_properties(q.device).multi_processor_count
-            splits = max(1, min((2 * sms + B * self.Hkv - 1) // (B * self.Hkv), pages))
+        splits = num_splits if num_splits > 0 else _fn("zs_decode_attention_default_splits")(B, self.Hkv, 64 * pages)
         splits = max(1, min(splits, max(1, pages)))
         nbytes = _fn("zs_decode_attention_workspace_bytes")(B, Hq, self.Hkv, splits)
         ws = torch.empty(max(nbytes // 4, 1), dtype=torch.float32, device=self.device)
