@@ -106,6 +106,18 @@ int zs_decode_attention(void* stream, const uint16_t* d_q, const void* const* k_
                         int D, int T_pad, int max_seqlen, float softmax_scale, int num_splits, float* d_ws,
                         size_t ws_bytes, uint16_t* d_out, int* splits_used, unsigned* d_err);
 
+/* Decode attention over an uncompressed, token-major K/V cache: d_k, d_v are
+ * [B][T_rows][Hkv][D] bf16 (T_rows % 64 == 0, D == 128), 16-byte aligned;
+ * everything else as zs_decode_attention (same kernel, every page read
+ * dense). Serves the reference's token-major compressed layout (FA
+ * flash_api.cpp:1512-1520, layout id 1) after zs_decompress has expanded it:
+ * a token-major compressed matrix of B*T_rows*Hkv rows x D columns decodes to
+ * exactly this [B][T_rows][Hkv][D] cache. */
+int zs_decode_attention_dense(void* stream, const uint16_t* d_q, const uint16_t* d_k, const uint16_t* d_v,
+                              const int* d_seqlens, int B, int Hq, int Hkv, int D, int T_rows, int max_seqlen,
+                              float softmax_scale, int num_splits, float* d_ws, size_t ws_bytes, uint16_t* d_out,
+                              int* splits_used, unsigned* d_err);
+
 /* Allocation-free decode attention (no counterpart in the reference).
  * For callers that cannot allocate device memory when they run attention
  * (code running inside an allocator's own hooks, or deployments that forbid

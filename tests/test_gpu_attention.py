@@ -71,6 +71,57 @@ def test_flash_attn_with_kvcache_descriptor_api():
     assert rel_l2(out.view(B, Hq, D), ref) <= TOL
 
 
+@pytest.mark.parametrize("B,T,Hkv,splits", [(2, 256, 8, 0), (3, 1000, 8, 0), (1, 4096, 8, 3), (2, 77, 4, 1),
+                                            (4, 1, 8, 0)])
+def test_flash_attn_with_kvcache_token_major_layout(B, T, Hkv, splits):
+    """Layout id 1: the K/V matrix is [B * T_pad * Hkv, D], row (b*T_pad+t)*Hkv+h."""
+    import zipserv_asplos26_b200 as zs
+    Hq, D = 32, 128
+    k = make_kv(B, T, Hkv, D, 40 + T)
+    v = make_kv(B, T, Hkv, D, 41 + T)
+    q = torch.randn(B, 1, Hq, D, device="cuda").to(torch.bfloat16)
+    kc = zs.compress_kv(k, layout="token_major")
+    vc = zs.compress_kv(v, layout="token_major")
+    t_pad = (T + 63) // 64 * 64
+    assert (kc.rows, kc.cols) == (B * t_pad * Hkv, D)
+    lens = torch.full((B,), T, dtype=torch.int32, device="cuda")
+    if B > 1:
+        lens[-1] = max(1, T // 3)   # ragged batch
+    out = zs.flash_attn_with_kvcache(q, cache_seqlens=lens, zipserv_k=kc.descriptor("token_major"),
+                                     zipserv_v=vc.descriptor("token_major"), zipserv_num_heads_k=Hkv,
+                                     num_splits=splits)
+    torch.cuda.synchronize()
+    ref = reference(q.view(B, Hq, D), k, v, lens.cpu(), 1.0 / math.sqrt(D)).to(torch.bfloat16)
+    assert out.shape == q.shape
+    assert rel_l2(out.view(B, Hq, D), ref) <= TOL
+
+
+@pytest.mark.parametrize("B,T,T_rows,splits", [(2, 200, 256, 0), (1, 64, 64, 1), (3, 1000, 1024, 5), (8, 4096, 4096, 0)])
+def test_decode_attention_dense_mode(B, T, T_rows, splits):
+    """The kernel with every page read from an uncompressed [B, T_rows, Hkv, D] cache."""
+    import zipserv_asplos26_b200 as zs
+    Hq, Hkv, D = 32, 8, 128
+    k = make_kv(B, T_rows, Hkv, D, 60 + T)
+    v = make_kv(B, T_rows, Hkv, D, 61 + T)
+    q = torch.randn(B, Hq, D, device="cuda").to(torch.bfloat16)
+    lens = torch.full((B,), T, dtype=torch.int32, device="cuda")
+    lens[0] = max(1, T - 63)
+    out = zs.decode_attention_dense(q, k, v, lens, num_splits=splits)
+    torch.cuda.synchronize()
+    ref = reference(q, k, v, lens.cpu(), 1.0 / math.sqrt(D)).to(torch.bfloat16)
+    assert rel_l2(out, ref) <= TOL
+
+
+def test_flash_attn_with_kvcache_rejects_mixed_layouts():
+    import zipserv_asplos26_b200 as zs
+    k = make_kv(1, 64, 8, 128, 3)
+    kc = zs.compress_kv(k)
+    q = torch.randn(1, 1, 32, 128, device="cuda").to(torch.bfloat16)
+    with pytest.raises(ValueError):
+        zs.flash_attn_with_kvcache(q, zipserv_k=kc.descriptor("by_kv_head"), zipserv_v=kc.descriptor("token_major"),
+                                   zipserv_num_heads_k=8)
+
+
 def test_decode_attention_kv_round_trip_is_lossless():
     import zipserv_asplos26_b200 as zs
     k = make_kv(2, 200, 8, 128, 9)

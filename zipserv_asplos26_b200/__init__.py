@@ -6,7 +6,9 @@ modules here are thin torch-facing wrappers over its C ABI."""
 from .codec import Compressed, analyze_exponents, compress, compress_host, decompress, to_device, zipgemm  # noqa: F401
 
 __all__ = ["Compressed", "analyze_exponents", "compress", "compress_host", "decompress", "to_device", "zipgemm"]
-from .attention import compress_kv, decode_attention, flash_attn_with_kvcache, pad_kv_by_kv_head  # noqa: E402,F401
+from .attention import (compress_kv, decode_attention, decode_attention_dense, flash_attn_with_kvcache,  # noqa: E402,F401
+                        pad_kv_by_kv_head, pad_kv_token_major)
 
-__all__ += ["compress_kv", "decode_attention", "flash_attn_with_kvcache", "pad_kv_by_kv_head"]
+__all__ += ["compress_kv", "decode_attention", "decode_attention_dense", "flash_attn_with_kvcache", "pad_kv_by_kv_head",
+            "pad_kv_token_major"]
 from . import store  # noqa: E402,F401  (save / load of compressed matrices)

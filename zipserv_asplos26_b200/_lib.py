@@ -28,6 +28,7 @@ _SIGS = {
     "zs_zipgemm": ([_P] * 8 + [_I, _I, _I, _P, _P, _I, _I, _I, _I, _P], _I),
     "zs_decode_attention_workspace_bytes": ([_I, _I, _I, _I], C.c_size_t),
     "zs_decode_attention_default_splits": ([_I, _I, _I], _I),
+    "zs_decode_attention_dense": ([_P, _P, _P, _P, _P] + [_I] * 6 + [C.c_float, _I, _P, C.c_size_t, _P, _P, _P], _I),
     "zs_decode_attention": ([_P, _P, _P, _P, _P, _P, _P] + [_I] * 6 + [C.c_float, _I, _P, C.c_size_t, _P, _P, _P],
                             _I),
 }

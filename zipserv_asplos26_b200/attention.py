@@ -34,10 +34,58 @@ def pad_kv_by_kv_head(x: torch.Tensor):
     return out.view(B * Hkv * t_pad, d_pad), B * Hkv * t_pad, t_pad
 
 
-def compress_kv(x: torch.Tensor, rule: str = "ext") -> Compressed:
-    """Compress a [B, T, Hkv, D] K or V cache in the head-major 64-token page layout."""
-    flat, _, _ = pad_kv_by_kv_head(x)
+def pad_kv_token_major(x: torch.Tensor):
+    """[B, T, Hkv, D] -> ([B*T_pad*Hkv, D] zero padded, T_pad): the reference's
+    token-major layout (row (b * T_pad + t) * Hkv + h; FA flash_api.cpp:1512-1520,
+    layout id 1), T padded to a multiple of 64 so the rows form whole tiles."""
+    B, T, Hkv, D = x.shape
+    if 64 % Hkv or D % 64:   # FA flash_api.cpp:1514-1520
+        raise ValueError("token-major layout needs Hkv dividing 64 and D a multiple of 64")
+    t_pad = (T + 63) // 64 * 64
+    out = torch.zeros((B, t_pad, Hkv, D), dtype=x.dtype, device=x.device)
+    out[:, :T] = x
+    return out.view(B * t_pad * Hkv, D), t_pad
+
+
+def compress_kv(x: torch.Tensor, rule: str = "ext", layout: str = "by_kv_head") -> Compressed:
+    """Compress a [B, T, Hkv, D] K or V cache: in the head-major 64-token page
+    layout (default), or in the token-major layout (layout="token_major")."""
+    if layout == "token_major":
+        flat, _ = pad_kv_token_major(x)
+    elif layout == "by_kv_head":
+        flat, _, _ = pad_kv_by_kv_head(x)
+    else:
+        raise ValueError(f"unknown layout {layout!r}")
     return compress(flat, rule=rule)
+
+
+def decode_attention_dense(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cache_seqlens: torch.Tensor,
+                           softmax_scale: Optional[float] = None, num_splits: int = 0,
+                           max_seqlen: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The decode-attention kernel on an uncompressed token-major cache:
+    q [B, Hq, D] (or [B, 1, Hq, D]), k / v [B, T_rows, Hkv, D] bf16 with
+    T_rows % 64 == 0 (every page read dense)."""
+    squeeze = q.dim() == 4
+    q3 = (q.reshape(q.shape[0], q.shape[-2], q.shape[-1]) if squeeze else q).contiguous()
+    B, Hq, D = q3.shape
+    if k.shape != v.shape or k.dim() != 4 or k.shape[0] != B or k.dtype != torch.bfloat16:
+        raise ValueError("k / v must be bf16 [B, T_rows, Hkv, D] tensors of the same shape")
+    t_rows, hk = k.shape[1], k.shape[2]
+    k, v = k.contiguous(), v.contiguous()
+    seq = cache_seqlens.to(device=q3.device, dtype=torch.int32).contiguous()
+    max_seqlen = t_rows if max_seqlen is None else min(max_seqlen, t_rows)
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    L = lib()
+    splits = num_splits if num_splits > 0 else L.zs_decode_attention_default_splits(B, hk, max_seqlen)
+    ws_bytes = L.zs_decode_attention_workspace_bytes(B, Hq, hk, splits)
+    ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device=q3.device)
+    if out is None:
+        out = torch.empty_like(q3)
+    check(L.zs_decode_attention_dense(torch.cuda.current_stream().cuda_stream, q3.data_ptr(), k.data_ptr(),
+                                      v.data_ptr(), seq.data_ptr(), B, Hq, hk, D, t_rows, max_seqlen, scale, splits,
+                                      ws.data_ptr(), ws_bytes, out.data_ptr(), None, None),
+          "zs_decode_attention_dense")
+    return out.view(q.shape) if squeeze else out
 
 
 def _ptrs_meta(c: Compressed):
@@ -105,18 +153,39 @@ def flash_attn_with_kvcache(q, k_cache=None, v_cache=None, cache_seqlens=None, s
     """Decode-attention entry with the reference's ZipServ keyword arguments.
 
     q is [B, 1, Hq, D]; zipserv_k / zipserv_v are descriptors as accepted by the
-    reference (dict with the 12 fields, or a sequence in that order, layout
-    "by_kv_head"). Only the compressed path is provided here."""
+    reference (dict with the 12 fields, or a sequence in that order; layout
+    "by_kv_head" or "token_major"). Only the compressed path is provided here."""
     if zipserv_k is None or zipserv_v is None:
         raise ValueError("zipserv_k and zipserv_v are required")
-    for d in (zipserv_k, zipserv_v):
-        if isinstance(d, dict) and d.get("layout", "by_kv_head") != "by_kv_head":
-            raise ValueError("only the by_kv_head layout is implemented")
+    layouts = {d.get("layout", "by_kv_head") if isinstance(d, dict) else "by_kv_head" for d in (zipserv_k, zipserv_v)}
+    if len(layouts) != 1 or not layouts <= {"by_kv_head", "token_major", 0, 1}:
+        raise ValueError("zipserv K and V must share one layout: by_kv_head (0) or token_major (1)")
+    layout = layouts.pop()
     hk = zipserv_num_heads_k if zipserv_num_heads_k else (k_cache.shape[2] if k_cache is not None else 0)
     if not hk:
         raise ValueError("zipserv_num_heads_k must be provided")
     k = _as_compressed(zipserv_k, q.device)
     v = _as_compressed(zipserv_v, q.device)
+    if layout in ("token_major", 1):
+        # Token-major pages interleave the KV heads (a 64-row tile holds 64 / Hkv
+        # tokens of every head), so the cache is expanded by the decompress
+        # kernel and attended with every page read dense: two stages of this
+        # library's kernels, where the reference decodes in its FA2 loop
+        # (FA flash_fwd_kernel.h:325-430).
+        B = q.shape[0]
+        if 64 % hk:   # FA flash_api.cpp:1514-1520
+            raise ValueError("token-major layout requires 64 % zipserv_num_heads_k == 0")
+        if k.rows % (B * hk) or k.rows != v.rows or k.cols != v.cols:
+            raise ValueError("token-major K/V rows must be B * T_pad * Hkv and agree")
+        t_rows = k.rows // (B * hk)
+        from .codec import decompress
+        kd = decompress(k).view(B, t_rows, hk, k.cols)
+        vd = decompress(v).view(B, t_rows, hk, v.cols)
+        if cache_seqlens is None:
+            cache_seqlens = torch.full((B,), t_rows, dtype=torch.int32, device=q.device)
+        elif not isinstance(cache_seqlens, torch.Tensor):
+            cache_seqlens = torch.full((B,), int(cache_seqlens), dtype=torch.int32, device=q.device)
+        return decode_attention_dense(q, kd, vd, cache_seqlens, softmax_scale, num_splits)
     if cache_seqlens is None:
         cache_seqlens = torch.full((q.shape[0],), k.rows // (q.shape[0] * hk), dtype=torch.int32, device=q.device)
     elif not isinstance(cache_seqlens, torch.Tensor):

@@ -77,6 +77,10 @@ struct AttnParams {
     int max_blocks, num_blocks;
     const uint16_t* tail_k;
     const uint16_t* tail_v;
+    // Dense mode (dense_all != 0): every page is read from tail_k / tail_v, laid
+    // out [B][dense_rows][Hkv][D] bf16 (token-major, uncompressed); the paged
+    // tails use dense_rows = 64.
+    int dense_all, dense_rows;
     // Paged pools' running maxima of a GT's padded {hf bytes, fallback elements}
     // (nullable): when given, every CTA sizes its page slots from them and
     // fits as many (2 or 3) as the launch's shared memory allows.
@@ -177,7 +181,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
     const int npages = (len + 63) >> 6;
     const bool has_tail = p.tail_k != nullptr && (len & 63) != 0;
     // the last page of a paged sequence with a dense tail is read from tail_k / tail_v
-    auto is_dense_page = [&](int g) { return has_tail && g == npages - 1; };
+    auto is_dense_page = [&](int g) { return p.dense_all || (has_tail && g == npages - 1); };
     const int pg0 = split * p.pages_per_split;
     const int np = max(0, min(npages, pg0 + p.pages_per_split) - pg0);
     const int G = p.G;
@@ -222,7 +226,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
                 const long long P = (long long)blk * p.Hkv + hk;
                 r.gt0 = 2 * P;
                 if (lane < 6) r.e = reinterpret_cast<const int2*>(So.page_off)[P * 3 + (lane % 3)];
-            } else if (lane < 6) {
+            } else if (lane < 6 && !p.dense_all) {
                 r.e = reinterpret_cast<const int2*>(So.gt_off)[(rb + pg0 + pi) * 2 + (lane % 3)];
             }
             return r;
@@ -303,10 +307,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             const uint32_t rows = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes + 16384u * (uint32_t)mat +
                                   8192u * (uint32_t)gc + 2048u * (uint32_t)mtile;
             if (is_dense_page(pg0 + pi)) {
-                // dense tail page: rows 16 mtile .. +15 (tokens), columns 64 gc .. +63 of
-                // K or V, zero past the sequence end, in the swizzled tile layout
-                const uint16_t* tb = (mat ? p.tail_v : p.tail_k) + ((size_t)b * 64 * p.Hkv + hk) * kAttnD + 64 * gc;
-                const int tl = len & 63;
+                // dense page (a paged sequence's tail, or every page in dense mode):
+                // rows 16 mtile .. +15 (tokens), columns 64 gc .. +63 of K or V, zero
+                // past the sequence end, in the swizzled tile layout
+                const int g = pg0 + pi;
+                const uint16_t* tb = (mat ? p.tail_v : p.tail_k) + ((size_t)b * p.dense_rows * p.Hkv + hk) * kAttnD +
+                                     (p.dense_all ? (size_t)64 * g * p.Hkv * kAttnD : 0) + 64 * gc;
+                const int tl = p.dense_all ? min(64, len - 64 * g) : (len & 63);
 #pragma unroll
                 for (int c = lane; c < 128; c += 32) {
                     const int rr = c >> 3, ch = c & 7, m = 16 * mtile + rr;
@@ -546,8 +553,10 @@ int attn_default_splits(int B, int Hkv, int max_pages) {
 static cudaError_t attention_core(cudaStream_t stream, const AttnCompressed& kc, const AttnCompressed& vc,
                                   const uint16_t* q, const int* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D,
                                   int T_pad, int max_seqlen, float softmax_scale, int num_splits, float* ws,
-                                  size_t ws_bytes, unsigned* err, int* splits_used, const AttnPaged* pg) {
+                                  size_t ws_bytes, unsigned* err, int* splits_used, const AttnPaged* pg,
+                                  const AttnDense* dn = nullptr) {
     if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D != kAttnD) return cudaErrorInvalidValue;
+    if (dn && (pg || !dn->k || !dn->v || !aligned16(dn->k) || !aligned16(dn->v))) return cudaErrorInvalidValue;
     if (!pg && (T_pad <= 0 || T_pad % 64)) return cudaErrorInvalidValue;
     const int G = Hq / Hkv;
     if (G > kAttnMaxG) return cudaErrorInvalidValue;
@@ -563,6 +572,7 @@ static cudaError_t attention_core(cudaStream_t stream, const AttnCompressed& kc,
     }
     const AttnCompressed* cs[2] = {&kc, &vc};
     for (const AttnCompressed* c : cs) {
+        if (dn) break;   // dense mode reads no compressed stream
         if (!c->b1 || !c->b2 || !c->b3 || !c->mt_off || (!pg && !c->gt_off)) return cudaErrorInvalidValue;
         if (!pg && (c->rows != B * Hkv * T_pad || c->cols != D)) return cudaErrorInvalidValue;
         if (c->max_hf < 0 || c->max_full < 0 || c->max_hf > 4096 + 15 || c->max_full > 4096 + 7)
@@ -593,15 +603,22 @@ static cudaError_t attention_core(cudaStream_t stream, const AttnCompressed& kc,
         p.num_blocks = pg->num_blocks;
         p.tail_k = pg->tail_k;
         p.tail_v = pg->tail_v;
+        p.dense_rows = 64;
         p.k_max = pg->k_max;
         p.v_max = pg->v_max;
+    }
+    if (dn) {
+        p.tail_k = dn->k;
+        p.tail_v = dn->v;
+        p.dense_all = 1;
+        p.dense_rows = T_pad;
     }
     p.q = q; p.seqlens = seqlens; p.out = out; p.ws = ws; p.err = err;
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.T_pad = T_pad; p.S = S;
     p.pages_per_split = (max_pages + S - 1) / S;
     p.scale_log2 = softmax_scale * 1.4426950408889634f;
-    const uint32_t hfc = round_up_u32((uint32_t)std::max(kc.max_hf, vc.max_hf), 16);
-    const uint32_t ffc = round_up_u32((uint32_t)std::max(kc.max_full, vc.max_full) * 2u, 16);
+    const uint32_t hfc = dn ? 16u : round_up_u32((uint32_t)std::max(kc.max_hf, vc.max_hf), 16);
+    const uint32_t ffc = dn ? 16u : round_up_u32((uint32_t)std::max(kc.max_full, vc.max_full) * 2u, 16);
     // compressed page slot per matrix: 3 x 1 KB bitmaps, 64 B median offsets, the
     // two GTs' hf stream (+16 B read slack) and fallback stream
     p.c_hf = 3072u + 64u;
@@ -706,6 +723,16 @@ cudaError_t launch_attention_paged(cudaStream_t stream, const AttnCompressed& kc
                                    float* ws, size_t ws_bytes, unsigned* err, int* splits_used) {
     return attention_core(stream, kc, vc, q, seqlens, out, B, Hq, Hkv, D, 64, max_seqlen, softmax_scale,
                           num_splits, ws, ws_bytes, err, splits_used, &pg);
+}
+
+cudaError_t launch_attention_dense(cudaStream_t stream, const uint16_t* k, const uint16_t* v, const uint16_t* q,
+                                   const int* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int T_rows,
+                                   int max_seqlen, float softmax_scale, int num_splits, float* ws, size_t ws_bytes,
+                                   unsigned* err, int* splits_used) {
+    const AttnCompressed none{};
+    const AttnDense dn{k, v};
+    return attention_core(stream, none, none, q, seqlens, out, B, Hq, Hkv, D, T_rows, max_seqlen, softmax_scale,
+                          num_splits, ws, ws_bytes, err, splits_used, nullptr, &dn);
 }
 
 size_t attn_noalloc_ws_bytes() { return kNoAllocWsFloats * sizeof(float); }

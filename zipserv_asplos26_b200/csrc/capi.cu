@@ -82,6 +82,14 @@ extern "C" int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_f
                               max_full, start_exp, d_x, d_c, M, N, K, split_k, d_err);
 }
 
+extern "C" int zs_decode_attention_dense(void* stream, const uint16_t* d_q, const uint16_t* d_k, const uint16_t* d_v,
+                                         const int* d_seqlens, int B, int Hq, int Hkv, int D, int T_rows,
+                                         int max_seqlen, float softmax_scale, int num_splits, float* d_ws,
+                                         size_t ws_bytes, uint16_t* d_out, int* splits_used, unsigned* d_err) {
+    return zs::launch_attention_dense((cudaStream_t)stream, d_k, d_v, d_q, d_seqlens, d_out, B, Hq, Hkv, D, T_rows,
+                                      max_seqlen, softmax_scale, num_splits, d_ws, ws_bytes, d_err, splits_used);
+}
+
 extern "C" int zs_decode_attention_default_splits(int B, int Hkv, int max_seqlen) {
     if (B <= 0 || Hkv <= 0 || max_seqlen < 0) return 1;
     return zs::attn_default_splits(B, Hkv, (max_seqlen + 63) / 64);

@@ -84,6 +84,17 @@ cudaError_t launch_attention_paged(cudaStream_t s, const AttnCompressed& k, cons
                                    int Hq, int Hkv, int D, int max_seqlen, float softmax_scale, int num_splits,
                                    float* ws, size_t ws_bytes, unsigned* err, int* splits_used);
 
+// Decode attention over an uncompressed token-major cache ([B][T_rows][Hkv][D]
+// bf16, T_rows % 64 == 0): the same kernel with every page read dense.
+struct AttnDense {
+    const uint16_t* k;
+    const uint16_t* v;
+};
+cudaError_t launch_attention_dense(cudaStream_t s, const uint16_t* k, const uint16_t* v, const uint16_t* q,
+                                   const int* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int T_rows,
+                                   int max_seqlen, float softmax_scale, int num_splits, float* ws, size_t ws_bytes,
+                                   unsigned* err, int* splits_used);
+
 size_t attn_noalloc_ws_bytes();
 cudaError_t launch_attention_noalloc(cudaStream_t s, const AttnCompressed& k, const AttnCompressed& v,
                                      const uint16_t* q, const int* seqlens, uint16_t* out, int B, int Hq, int Hkv,
