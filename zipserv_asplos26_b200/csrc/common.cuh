@@ -382,10 +382,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
 // The result is four 32-bit words = 8 bf16 in column order, i.e. exactly the
 // 16 bytes of the row segment.
 //
-// Work per row: the code nibbles X (nibble j = code of column j) come from a
-// 256-entry bit->nibble spread table; the prefix-popcount selector for the
-// packed sign/mantissa bytes is spread(indicator) * 0x11111110; everything else
-// is byte permutes (prmt) and 3-input logic ops.
+// Work per row: the code nibbles X (nibble j = code of column j) are built from
+// the three bitmap bytes with byte permutes of a constant (decode_row_words);
+// the prefix-popcount selector for the packed sign/mantissa bytes is
+// spread(indicator) * 0x11111110; everything else is byte permutes (prmt) and
+// 3-input logic ops.
 // ---------------------------------------------------------------------------
 struct DecodeTables {
     uint32_t thb0, thb1, tlb0, tlb1;
@@ -401,13 +402,6 @@ __host__ __device__ inline DecodeTables make_decode_tables(int start_exp) {
     }
     t.thb0 = hb[0]; t.thb1 = hb[1]; t.tlb0 = lb[0]; t.tlb1 = lb[1];
     return t;
-}
-
-// spread8[b]: nibble j = bit j of b.
-__host__ __device__ inline uint32_t spread8_value(uint32_t b) {
-    uint32_t r = 0;
-    for (int j = 0; j < 8; ++j) r |= ((b >> j) & 1u) << (4 * j);
-    return r;
 }
 
 // Shared-memory accesses on 32-bit shared addresses. The loads carry no memory
@@ -452,53 +446,10 @@ __device__ __forceinline__ uint32_t lop_or_and(uint32_t a, uint32_t mask, uint32
     return (a & mask) | b;  // compiles to a single LOP3
 }
 
-// Spread table in shared memory, one private copy per lane (bank): entry b of
-// lane l is the word at byte offset b * 128 + l * 4.
-constexpr int kLutCopies = 32;
-constexpr int kLutWords = 256 * kLutCopies;
-
-__device__ __forceinline__ uint32_t spread8_fast(uint32_t x) {
-    x = (x | (x << 12)) & 0x000F000Fu;
-    x = (x | (x << 6)) & 0x03030303u;
-    x = (x | (x << 3)) & 0x11111111u;
-    return x;
-}
-
-__device__ __forceinline__ void fill_spread_table(uint32_t* lut, int tid, int nthreads) {
-    for (int i = tid; i < kLutWords; i += nthreads) lut[i] = spread8_fast((uint32_t)(i / kLutCopies));
-}
-
-// Decode the high-frequency elements of one small-tile row (8 elements).
-// c1, c2, c3: clean bytes of the three bitmaps for this row. lut_lane: shared
-// address of this lane's table copy. win: shared address of the row's first hf
-// byte (the stream base is 16-byte aligned; >= 12 bytes readable from win & ~3).
-// Fallback positions (code 0) receive junk; the caller patches them.
-__device__ __forceinline__ void decode_row_hf(uint32_t c1, uint32_t c2, uint32_t c3, uint32_t lut_lane,
-                                              uint32_t win, const DecodeTables& t, uint32_t (&o)[4]) {
-    const uint32_t s1 = lds32(lut_lane + (c1 << 7)), s2 = lds32(lut_lane + (c2 << 7)),
-                   s3 = lds32(lut_lane + (c3 << 7));
-    const uint32_t X = s1 + (s2 << 1) + (s3 << 2);        // code nibbles
-    const uint32_t sel = (s1 | s2 | s3) * 0x11111110u;    // hf-before-j nibbles
-    const uint32_t wa = win & ~3u;
-    const uint32_t sh = (win & 3u) * 8u;
-    const uint32_t q0 = lds32(wa), q1 = lds32(wa + 4), q2 = lds32(wa + 8);
-    const uint32_t lo = __funnelshift_r(q0, q1, sh);
-    const uint32_t hi = __funnelshift_r(q1, q2, sh);
-    const uint32_t s_lo = prmt(lo, hi, sel);
-    const uint32_t s_hi = prmt(lo, hi, sel >> 16);
-    const uint32_t hb_lo = lop_or_and(s_lo, 0x80808080u, prmt(t.thb0, t.thb1, X));
-    const uint32_t hb_hi = lop_or_and(s_hi, 0x80808080u, prmt(t.thb0, t.thb1, X >> 16));
-    const uint32_t lb_lo = lop_or_and(s_lo, 0x7F7F7F7Fu, prmt(t.tlb0, t.tlb1, X));
-    const uint32_t lb_hi = lop_or_and(s_hi, 0x7F7F7F7Fu, prmt(t.tlb0, t.tlb1, X >> 16));
-    o[0] = prmt(lb_lo, hb_lo, 0x5140);
-    o[1] = prmt(lb_lo, hb_lo, 0x7362);
-    o[2] = prmt(lb_hi, hb_hi, 0x5140);
-    o[3] = prmt(lb_hi, hb_hi, 0x7362);
-}
-
-// Table-free variant of decode_row_hf for callers that hold the three bitmap
-// words of a small tile's row half (w1, w2, w3: rows 4h .. 4h+3, one byte per
-// row) and decode row r (0..3) of them. The spread of a bitmap byte c (nibble
+// Decode the high-frequency elements of one small-tile row (8 elements) from
+// the three bitmap words of a small tile's row half (w1, w2, w3: rows 4h ..
+// 4h+3, one byte per row), row r (0..3) of them; fallback positions (code 0)
+// receive junk that the caller patches. The spread of a bitmap byte c (nibble
 // j = bit j) has byte k = {0x00, 0x01, 0x10, 0x11}[(c >> 2k) & 3], so one
 // byte permute of the constant 0x11100100 produces it from a selector whose
 // nibble k is bit group k of c; the selectors of bitmaps 1 and 2 are built
