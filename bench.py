@@ -6,7 +6,10 @@ TCA-TBE compressed, X N=128 tokens ~ N(0, 1), SplitK=1, fp32 accumulate).
 One step = one config-2 GEMM. Multi-GPU (torchrun): row-parallel strong
 scaling, as a tensor-parallel O / down projection runs -- rank r holds columns
 [K r / N, K (r+1) / N) of W (its own compressed shard, seeded by r) and of X,
-and an NCCL all-reduce sums the partial Ys inside every step. The timed region
+and the all-reduce of the partial Ys is fused into the ZipGEMM (each CTA
+stores its rows into every rank's exchange buffer over NVLink and sums the
+ranks' rows once they have landed); `unfused_nccl_us_per_step` times the same
+steps as ZipGEMM + NCCL all-reduce, as context. The timed region
 is K CUDA-graph replayed steps bracketed by barrier + synchronize; time = max
 over ranks. Before the headline line, the config-4 Llama-70B layer at tp = N
 is printed (one line per token count).
@@ -516,7 +519,8 @@ def run_roundtrip(args):
 def tp70b_lines(world, rank, dev, reps=20):
     """Config 4: one Llama-3.1-70B decoder layer's four weight GEMMs,
     tensor-parallel over the ranks (QKV / gate_up column-parallel, O / down
-    row-parallel + NCCL all-reduce), captured in one CUDA graph per N; per-layer
+    row-parallel with the all-reduce fused into the ZipGEMM), captured in one
+    CUDA graph per N; per-layer
     device time = max over ranks. Also times GPU compression of this rank's four
     shards. Returns one dict per N (printed by rank 0)."""
     import torch
@@ -524,7 +528,7 @@ def tp70b_lines(world, rank, dev, reps=20):
 
     import zipserv_asplos26_b200 as zs
     from zipserv_asplos26_b200.tp import LLAMA70B_SHAPES, TPLayerGemms
-    layer = TPLayerGemms(LLAMA70B_SHAPES, seed=0, device=dev)
+    layer = TPLayerGemms(LLAMA70B_SHAPES, seed=0, device=dev, fused=world > 1)
     comp_ms, in_bytes = 0.0, 0
     for lin in layer.layers.values():
         w = (torch.randn(lin.out_features, lin.in_features, device=dev) * 0.02).to(torch.bfloat16)
@@ -570,8 +574,9 @@ def tp70b_lines(world, rank, dev, reps=20):
                     "per_rank_compressed_MB": round(cb / 1e6, 2), "per_rank_GBps": round(cb / t.item() / 1e3, 1),
                     "compress_layer_ms": round(comp_ms, 2),
                     "compress_GBps_bf16_in": round(in_bytes / comp_ms / 1e6, 1),
-                    "note": "4 projections per layer incl. 2 NCCL all-reduces (bf16 sum), one CUDA graph of "
-                            f"{reps} layers, max over ranks"})
+                    "note": "4 projections per layer" + (
+                        ", O and down with the all-reduce fused into the ZipGEMM (NVLink peer stores)"
+                        if world > 1 else "") + f", one CUDA graph of {reps} layers, max over ranks"})
         del g
     return out
 
@@ -715,10 +720,15 @@ def main():
         dist.all_reduce(tb)
     job_bytes = tb.item()                            # all ranks' algorithmic bytes per step
 
+    if world > 1:
+        from zipserv_asplos26_b200.tp import AllReduceBuffers, zipgemm_allreduce
+        bufs = AllReduceBuffers(M_, N_, device=dev)
+
     def step(i, xin, yout):
-        zs.zipgemm(comps[i % n_sets], xin, out=yout)
-        if world > 1:
-            dist.all_reduce(yout, op=dist.ReduceOp.SUM)
+        if world > 1:   # the all-reduce of Y fused into the ZipGEMM (NVLink peer stores)
+            zipgemm_allreduce(comps[i % n_sets], xin, bufs, out=yout)
+        else:
+            zs.zipgemm(comps[i % n_sets], xin, out=yout)
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
@@ -745,6 +755,25 @@ def main():
         kb.record(stream)
         kb.synchronize()
         gemm_ms = ka.elapsed_time(kb) / K
+
+        # context for N > 1: the same steps unfused (ZipGEMM, then an NCCL all-reduce of Y)
+        nccl_ms = 0.0
+        if world > 1:
+            ngraph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ngraph, stream=stream):
+                for i in range(K):
+                    zs.zipgemm(comps[i % n_sets], x, out=ys[i % 2])
+                    dist.all_reduce(ys[i % 2], op=dist.ReduceOp.SUM)
+            ngraph.replay()
+            stream.synchronize()
+            dist.barrier()
+            na, nb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            na.record(stream)
+            ngraph.replay()
+            nb.record(stream)
+            nb.synchronize()
+            nccl_ms = na.elapsed_time(nb) / K
+            del ngraph
 
         # Load the GPU for about a second while the clock sampler runs. Every rank
         # must replay the graph the same number of times (its collectives pair up
@@ -829,10 +858,10 @@ def main():
         bb.record(stream)
         bb.synchronize()
         e2e_ms = a.elapsed_time(bb)
-    t = torch.tensor([ms_total, e2e_ms, gemm_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms_total, e2e_ms, gemm_ms, nccl_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total, e2e_ms, gemm_ms = t.tolist()
+    ms_total, e2e_ms, gemm_ms, nccl_ms = t.tolist()
     ms_step = ms_total / K
     peak, peak_kind = peaks()
     achieved = nbytes / (gemm_ms / 1e3) / 1e9
@@ -848,7 +877,7 @@ def main():
             print(json.dumps(line), flush=True)
         par = ("single GPU" if world == 1 else
                f"row-parallel tp{world}: W and X split by K over the ranks (own compressed shard per rank), "
-               "NCCL all-reduce (bf16 sum) of Y in every step")
+               "the all-reduce (bf16 partials summed in fp32) of Y fused into the ZipGEMM in every step")
         line = {
             "metric": METRIC, "value": job_bytes * K / (ms_total / 1e3) / 1e9, "unit": "GB/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
@@ -871,6 +900,7 @@ def main():
                             "calls captured in one CUDA graph and replayed"},
             "dense_bf16_us": dense_us,
             "speedup_vs_dense_bf16": (dense_us / (gemm_ms * 1e3)) if dense_us else None,
+            "unfused_nccl_us_per_step": (nccl_ms * 1e3) if world > 1 else None,
             "gpu_launches": K,
             "clocks": clocks,
         }

@@ -77,6 +77,48 @@ int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const 
                int max_hf, int max_full, int start_exp, const uint16_t* d_x, uint16_t* d_c, int M, int N,
                int K, int split_k, unsigned* d_err);
 
+/* Row-parallel ZipGEMM with the all-reduce of its output fused into the
+ * kernel's epilogue. New relative to the reference, which has no collectives;
+ * it replaces zs_zipgemm followed by an NCCL all-reduce of d_c when W is split
+ * by K over `world` GPUs (a tensor-parallel O or down projection).
+ *
+ * Every rank calls it with its own compressed K shard of W (M x K), its K
+ * slice of X (N x K) and the same M and N; on return d_c holds, on every rank,
+ * bf16(sum over ranks j in order 0..world-1 of bf16(W_j X_j^T)), bit-identical
+ * across ranks. Each CTA stores its finished rows over NVLink into every
+ * peer's exchange buffer, as 8-byte words of two bf16 values and the call's
+ * flag, and polls (bounded, about 2 s; then error bit 1 in *d_err) its own
+ * buffer until the peers' words of the same rows carry the flag.
+ *
+ * peer_bufs: host array of `world` device pointers: rank j's exchange buffer
+ * of zs_zipgemm_allreduce_buffer_bytes(M, N, world) bytes, zeroed, opened on
+ * this GPU (zs_peer_alloc on its owner, zs_peer_open here; own buffer at
+ * [rank]), 256-byte aligned. d_epoch: this rank's zs_zipgemm_allreduce_counters
+ * (M, N) unsigned counters (exchanges completed per tile), zeroed once, kept
+ * between calls. All ranks must
+ * issue the same sequence of calls with the same M, N. The grid must be
+ * resident in one wave (it waits on the peers' CTAs of the same tile):
+ * cudaErrorInvalidValue when M / 128 tiles exceed the co-resident clusters,
+ * or when K < 128. world: 2..8. */
+size_t zs_zipgemm_allreduce_buffer_bytes(int M, int N, int world);
+size_t zs_zipgemm_allreduce_counters(int M, int N);
+int zs_zipgemm_allreduce(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const uint64_t* d_b1,
+                         const uint64_t* d_b2, const uint64_t* d_b3, const int* d_mt_off, const int* d_gt_off,
+                         int max_hf, int max_full, int start_exp, const uint16_t* d_x, uint16_t* d_c, int M, int N,
+                         int K, int world, int rank, void* const* peer_bufs, unsigned* d_epoch, unsigned* d_err);
+
+/* Exchange buffers shared between the GPUs of one node (CUDA IPC). New
+ * relative to the reference. zs_peer_alloc: cudaMalloc `bytes` on the current
+ * device, zero them, and write the IPC handle (zs_peer_handle_bytes() bytes)
+ * that other processes pass to zs_peer_open; free with zs_peer_free.
+ * zs_peer_open maps a peer's buffer into this process (close with
+ * zs_peer_close). */
+size_t zs_peer_handle_bytes(void);
+int zs_peer_alloc(size_t bytes, void** d_ptr, void* ipc_handle);
+int zs_peer_open(const void* ipc_handle, void** d_ptr);
+int zs_peer_close(void* d_ptr);
+int zs_peer_free(void* d_ptr);
+
 /* The split-KV factor zs_decode_attention picks when num_splits <= 0, for B
  * sequences of Hkv KV heads and up to max_seqlen tokens (a grid that fills the
  * SMs in few, full waves). New relative to the reference, whose FlashAttention

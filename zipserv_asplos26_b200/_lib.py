@@ -26,6 +26,14 @@ _SIGS = {
     "zs_encode": ([_P, _P, _I, _I, _P] + [_P] * 10, _I),
     "zs_decompress": ([_P] * 8 + [_I, _I, _I, _P, _I, _I, _P], _I),
     "zs_zipgemm": ([_P] * 8 + [_I, _I, _I, _P, _P, _I, _I, _I, _I, _P], _I),
+    "zs_zipgemm_allreduce_buffer_bytes": ([_I, _I, _I], C.c_size_t),
+    "zs_zipgemm_allreduce_counters": ([_I, _I], C.c_size_t),
+    "zs_zipgemm_allreduce": ([_P] * 8 + [_I, _I, _I, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P], _I),
+    "zs_peer_handle_bytes": ([], C.c_size_t),
+    "zs_peer_alloc": ([C.c_size_t, _P, _P], _I),
+    "zs_peer_open": ([_P, _P], _I),
+    "zs_peer_close": ([_P], _I),
+    "zs_peer_free": ([_P], _I),
     "zs_decode_attention_workspace_bytes": ([_I, _I, _I, _I], C.c_size_t),
     "zs_decode_attention_default_splits": ([_I, _I, _I], _I),
     "zs_decode_attention_dense": ([_P, _P, _P, _P, _P] + [_I] * 6 + [C.c_float, _I, _P, C.c_size_t, _P, _P, _P], _I),

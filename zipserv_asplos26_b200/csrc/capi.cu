@@ -1,5 +1,6 @@
 // C ABI (include/zipserv_b200.h) and the reference's GPU C++ ABI
 // (include/L_API.cuh, same mangled names as the reference build/L_API.cuh).
+#include <cstring>
 #include <cstdlib>
 #include <new>
 #include <vector>
@@ -81,6 +82,53 @@ extern "C" int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_f
     return zs::launch_zipgemm((cudaStream_t)stream, d_sm, d_full, d_b1, d_b2, d_b3, d_mt_off, d_gt_off, max_hf,
                               max_full, start_exp, d_x, d_c, M, N, K, split_k, d_err);
 }
+
+extern "C" size_t zs_zipgemm_allreduce_buffer_bytes(int M, int N, int world) {
+    return zs::zipgemm_allreduce_buffer_bytes(M, N, world);
+}
+
+extern "C" size_t zs_zipgemm_allreduce_counters(int M, int N) { return zs::zipgemm_allreduce_counters(M, N); }
+
+extern "C" int zs_zipgemm_allreduce(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const uint64_t* d_b1,
+                                    const uint64_t* d_b2, const uint64_t* d_b3, const int* d_mt_off,
+                                    const int* d_gt_off, int max_hf, int max_full, int start_exp, const uint16_t* d_x,
+                                    uint16_t* d_c, int M, int N, int K, int world, int rank, void* const* peer_bufs,
+                                    unsigned* d_epoch, unsigned* d_err) {
+    return zs::launch_zipgemm_allreduce((cudaStream_t)stream, d_sm, d_full, d_b1, d_b2, d_b3, d_mt_off, d_gt_off,
+                                        max_hf, max_full, start_exp, d_x, d_c, M, N, K, world, rank, peer_bufs,
+                                        d_epoch, d_err);
+}
+
+extern "C" int zs_peer_alloc(size_t bytes, void** d_ptr, void* ipc_handle) {
+    if (!d_ptr || !ipc_handle || bytes == 0) return cudaErrorInvalidValue;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return e;
+    e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return e;
+    }
+    memcpy(ipc_handle, &h, sizeof(h));
+    *d_ptr = p;
+    return cudaSuccess;
+}
+
+extern "C" int zs_peer_open(const void* ipc_handle, void** d_ptr) {
+    if (!ipc_handle || !d_ptr) return cudaErrorInvalidValue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    return cudaIpcOpenMemHandle(d_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+extern "C" int zs_peer_close(void* d_ptr) { return cudaIpcCloseMemHandle(d_ptr); }
+
+extern "C" int zs_peer_free(void* d_ptr) { return cudaFree(d_ptr); }
+
+extern "C" size_t zs_peer_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
 
 extern "C" int zs_decode_attention_dense(void* stream, const uint16_t* d_q, const uint16_t* d_k, const uint16_t* d_v,
                                          const int* d_seqlens, int B, int Hq, int Hkv, int D, int T_rows,

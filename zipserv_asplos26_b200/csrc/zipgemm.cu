@@ -100,6 +100,14 @@ struct GemmParams {
     uint32_t hf_area, full_area;    // bytes (hf) / elements (fallback) one GT row of a chunk may hold
     uint32_t tmem_cols;
     unsigned* err;
+    // Row-parallel all-reduce fused into the epilogue (world > 1): recv[j] is
+    // rank j's exchange buffer [2][world][Ntot][M / 2] words of (bf16 x 2,
+    // flag) (this rank's own at [rank]); epoch (local) counts the exchanges
+    // each tile has completed. Column chunk n0 of Ntot; flag_base offsets the
+    // chunk's counters.
+    int world, rank, Ntot, n0, flag_base;
+    uint16_t* recv[8];
+    unsigned* epoch;
     int debug;   // diagnostic builds only (-DZS_TRACE): experiment bits
 };
 
@@ -189,6 +197,105 @@ __device__ __forceinline__ void cluster_reduce(const GemmParams& p, uint32_t par
             }
         }
     }
+}
+
+// The split-tile sum fused with the row-parallel all-reduce over `world` GPUs.
+// CTA r of the cluster sums its rows of the S partial tiles (as cluster_reduce)
+// and rounds this rank's result to bf16 (what an all-reduce of the bf16
+// partial Ys would receive). Each 8-byte word it sends holds two bf16 values
+// and the tile's exchange number (flag = exchanges completed + 1), so a word
+// is complete the moment it is visible: it stores its words into slot `rank`
+// of every peer's exchange buffer over NVLink, then polls the peers' words in
+// its own buffer until their flags match (bounded), and adds the `world`
+// partials in rank order in fp32 before writing bf16 C, so every rank
+// computes bit-identical Y. No fence, counter or barrier is needed. The
+// buffer has two halves, chosen by the parity of the exchange number: a rank
+// can be one exchange ahead of a peer that is still reading, never two (its
+// next exchange needs that peer's next words, which the peer stores only
+// after it has read this exchange's).
+constexpr int kArMaxItems = 8;   // items (4 rows x 1 column) per thread: BN * 32 / S / kGemmThreads <= 7
+template <int S>
+__device__ __forceinline__ void cluster_reduce_allreduce(const GemmParams& p, uint32_t part, int T, int r, int tid) {
+    constexpr int R = 128 / S, R4 = R / 4;
+    const int items = p.BN * R4;
+    const int fidx = p.flag_base + T * S + r;
+    const unsigned cnt = p.epoch[fidx];
+    const unsigned long long flag = (unsigned long long)(cnt + 1u) << 32;
+    const size_t slot = (size_t)p.Ntot * (size_t)p.M / 2;   // 8-byte words of one rank's partial
+    const size_t half = (size_t)(cnt & 1u) * (size_t)p.world * slot;
+    uint2 own[kArMaxItems];
+#pragma unroll
+    for (int t = 0; t < kArMaxItems; ++t) {
+        const int e = tid + t * kGemmThreads;
+        if (e >= items) break;
+        const int col = e / R4, m4 = R * r + 4 * (e - col * R4);
+        const uint32_t a = part + 4u * (uint32_t)(col * 128 + m4);
+        float4 v[S];
+#pragma unroll
+        for (int j = 0; j < S; ++j) v[j] = ld_dsmem_f4(mapa_shared(a, (uint32_t)j));
+        float4 acc = v[0];
+#pragma unroll
+        for (int j = 1; j < S; ++j) {
+            acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
+        }
+        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+        own[t].x = *reinterpret_cast<uint32_t*>(&lo);
+        own[t].y = *reinterpret_cast<uint32_t*>(&hi);
+        const int m = 128 * T + m4;
+        if (col < p.N && m < p.M) {
+            const size_t off = half + (size_t)p.rank * slot + ((size_t)(p.n0 + col) * p.M + m) / 2;
+            for (int j = 0; j < p.world; ++j) {
+                if (j == p.rank) continue;
+                volatile unsigned long long* dst = reinterpret_cast<unsigned long long*>(p.recv[j]) + off;
+                dst[0] = flag | own[t].x;
+                dst[1] = flag | own[t].y;
+            }
+        }
+    }
+    bool ok = true;
+    const long long t0 = clock64();
+#pragma unroll
+    for (int t = 0; t < kArMaxItems; ++t) {
+        const int e = tid + t * kGemmThreads;
+        if (e >= items) break;
+        const int col = e / R4, m4 = R * r + 4 * (e - col * R4);
+        const int m = 128 * T + m4;
+        if (col >= p.N || m >= p.M) continue;
+        const volatile unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.recv[p.rank]) + half +
+                                                 ((size_t)(p.n0 + col) * p.M + m) / 2;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < p.world; ++j) {
+            uint2 q = own[t];
+            if (j != p.rank) {
+                unsigned long long w0, w1;
+                for (uint32_t it = 0;; ++it) {
+                    w0 = src[(size_t)j * slot];
+                    w1 = src[(size_t)j * slot + 1];
+                    if ((w0 & 0xFFFFFFFF00000000ull) == flag && (w1 & 0xFFFFFFFF00000000ull) == flag) break;
+                    if (!ok || ((it & 255) == 255 && clock64() - t0 > kWaitLimitCycles)) {
+                        if (ok && p.err) atomicOr(p.err, kErrWaitTimeout);
+                        ok = false;
+                        break;
+                    }
+                }
+                q.x = (uint32_t)w0;
+                q.y = (uint32_t)w1;
+            }
+            const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
+            const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
+            if (j == 0) {
+                acc = make_float4(lo.x, lo.y, hi.x, hi.y);
+            } else {
+                acc.x += lo.x; acc.y += lo.y; acc.z += hi.x; acc.w += hi.y;
+            }
+        }
+        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(p.C + (size_t)col * p.M + m) = pk;
+    }
+    if (tid == 0) p.epoch[fidx] = cnt + 1u;
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -486,10 +593,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         cluster_sync();   // every partial of the cluster is parked
         if (tid == 0) ZS_STAMP(5);
         grid_dep_wait();  // C may still be in use by the previous grid
-        switch (p.S) {
-            case 2: cluster_reduce<2>(p, smem0 + p.off_part, T, r, tid); break;
-            case 4: cluster_reduce<4>(p, smem0 + p.off_part, T, r, tid); break;
-            default: cluster_reduce<8>(p, smem0 + p.off_part, T, r, tid); break;
+        if (p.world > 1) {
+            switch (p.S) {
+                case 2: cluster_reduce_allreduce<2>(p, smem0 + p.off_part, T, r, tid); break;
+                case 4: cluster_reduce_allreduce<4>(p, smem0 + p.off_part, T, r, tid); break;
+                default: cluster_reduce_allreduce<8>(p, smem0 + p.off_part, T, r, tid); break;
+            }
+        } else {
+            switch (p.S) {
+                case 2: cluster_reduce<2>(p, smem0 + p.off_part, T, r, tid); break;
+                case 4: cluster_reduce<4>(p, smem0 + p.off_part, T, r, tid); break;
+                default: cluster_reduce<8>(p, smem0 + p.off_part, T, r, tid); break;
+            }
         }
         if (tid == 0) ZS_STAMP(7);
         cluster_sync();   // peers may still be reading this CTA's partial
@@ -572,12 +687,13 @@ static cudaError_t dev_setup(int dev, DevInfo* out) {
 
 // K split: the cluster size S in {1, 2, 4, 8} that minimises waves x units per
 // CTA (plus one unit's worth for the partial-tile exchange when S > 1).
-static int choose_split(const DevInfo& di, long long tiles, int gtk) {
-    int best = 1;
+static int choose_split(const DevInfo& di, long long tiles, int gtk, int min_s = 1) {
+    int best = 0;
     double best_cost = 1e30;
     for (int i = 0; i < 4; ++i) {
         const int S = 1 << i;
-        if (S > gtk || di.clusters[i] <= 0) continue;
+        if (S < min_s || S > gtk || di.clusters[i] <= 0) continue;
+        if (min_s > 1 && tiles > di.clusters[i]) continue;   // fused all-reduce: one wave only
         const long long waves = (tiles + di.clusters[i] - 1) / di.clusters[i];
         const double cost = (double)waves * (double)((gtk + S - 1) / S) + (S > 1 ? 1.0 : 0.0);
         if (cost < best_cost - 1e-9) { best_cost = cost; best = S; }
@@ -595,7 +711,16 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, GemmPara
     p.gtk = p.K / kGT;
     p.mgt = p.M / kGT;
     const long long tiles = (p.M + 127) / 128;
-    p.S = choose_split(di, tiles, p.gtk);
+    // The fused all-reduce sums the split tiles in the cluster epilogue (S >= 2)
+    // and waits there for the other GPUs' CTAs of the same tile, so the whole
+    // grid must be resident at once (one wave).
+    p.S = choose_split(di, tiles, p.gtk, p.world > 1 ? 2 : 1);
+    if (p.S == 0) return cudaErrorInvalidValue;
+    if (p.world > 1) {
+        int li = 0;
+        while ((1 << li) < p.S) ++li;
+        if (tiles > di.clusters[li]) return cudaErrorInvalidValue;
+    }
     p.tmem_cols = 32;
     while (p.tmem_cols < (uint32_t)p.BN) p.tmem_cols <<= 1;
 
@@ -699,10 +824,10 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, GemmPara
     return cudaLaunchKernelEx(&cfg, zipgemm_kernel, maps, p);
 }
 
-cudaError_t launch_zipgemm(cudaStream_t stream, const uint8_t* sm, const uint16_t* full, const uint64_t* b1,
-                           const uint64_t* b2, const uint64_t* b3, const int* mt_off, const int* gt_off,
-                           int max_hf, int max_full, int start_exp, const uint16_t* X, uint16_t* C, int M, int N,
-                           int K, int split_k, unsigned* err) {
+static cudaError_t zipgemm_impl(cudaStream_t stream, const uint8_t* sm, const uint16_t* full, const uint64_t* b1,
+                                const uint64_t* b2, const uint64_t* b3, const int* mt_off, const int* gt_off,
+                                int max_hf, int max_full, int start_exp, const uint16_t* X, uint16_t* C, int M,
+                                int N, int K, int split_k, unsigned* err, const PeerExchange* px) {
     // split_k is accepted for the reference signature; the K split is chosen
     // from the shape and the SM count.
     if (M <= 0 || N <= 0 || K <= 0 || (M % 64) || (K % 64)) return cudaErrorInvalidValue;
@@ -723,15 +848,63 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const uint8_t* sm, const uint16_
     p.sm = sm; p.full = full; p.b1 = b1; p.b2 = b2; p.b3 = b3; p.mt_off = mt_off; p.gt_off = gt_off;
     p.start_exp = start_exp & 0xFF;
     p.M = M; p.K = K; p.err = err;
+    p.world = 1;
+    if (px) {
+        p.world = px->world;
+        p.rank = px->rank;
+        p.Ntot = N;
+        p.epoch = px->epoch;
+        for (int j = 0; j < px->world; ++j) p.recv[j] = px->recv[j];
+    }
     // N > 256 runs as column chunks of 256 (each re-decodes W; such N are
     // tensor-bound, so the repeated decode is a small share of the time)
-    for (int n0 = 0; n0 < N; n0 += 256) {
+    const int tiles = (M + 127) / 128;
+    for (int n0 = 0, chunk = 0; n0 < N; n0 += 256, ++chunk) {
         GemmParams q = p;
         q.N = std::min(256, N - n0);
         q.C = C + (size_t)n0 * M;
+        q.n0 = n0;
+        q.flag_base = chunk * tiles * 8;
         ZS_RETURN_IF_ERR(launch_chunk(stream, di, q, X + (size_t)n0 * K, max_hf, max_full));
     }
     return cudaSuccess;
+}
+
+cudaError_t launch_zipgemm(cudaStream_t stream, const uint8_t* sm, const uint16_t* full, const uint64_t* b1,
+                           const uint64_t* b2, const uint64_t* b3, const int* mt_off, const int* gt_off,
+                           int max_hf, int max_full, int start_exp, const uint16_t* X, uint16_t* C, int M, int N,
+                           int K, int split_k, unsigned* err) {
+    return zipgemm_impl(stream, sm, full, b1, b2, b3, mt_off, gt_off, max_hf, max_full, start_exp, X, C, M, N, K,
+                        split_k, err, nullptr);
+}
+
+size_t zipgemm_allreduce_counters(int M, int N) {
+    if (M <= 0 || N <= 0) return 0;
+    return (size_t)((N + 255) / 256) * (size_t)((M + 127) / 128) * 8;
+}
+
+size_t zipgemm_allreduce_buffer_bytes(int M, int N, int world) {
+    if (M <= 0 || N <= 0 || world < 2 || world > 8) return 0;
+    return 2ull * (size_t)world * (size_t)N * (size_t)M * 4ull;   // 2 halves x world slots x M N / 2 words
+}
+
+cudaError_t launch_zipgemm_allreduce(cudaStream_t stream, const uint8_t* sm, const uint16_t* full,
+                                     const uint64_t* b1, const uint64_t* b2, const uint64_t* b3, const int* mt_off,
+                                     const int* gt_off, int max_hf, int max_full, int start_exp, const uint16_t* X,
+                                     uint16_t* C, int M, int N, int K, int world, int rank, void* const* peer_bufs,
+                                     unsigned* epoch, unsigned* err) {
+    if (world < 2 || world > 8 || rank < 0 || rank >= world || !peer_bufs || !epoch) return cudaErrorInvalidValue;
+    if (M <= 0 || N <= 0) return cudaErrorInvalidValue;
+    PeerExchange px;
+    px.world = world;
+    px.rank = rank;
+    px.epoch = epoch;
+    for (int j = 0; j < world; ++j) {
+        if (!peer_bufs[j] || (reinterpret_cast<uintptr_t>(peer_bufs[j]) & 255u)) return cudaErrorInvalidValue;
+        px.recv[j] = reinterpret_cast<uint16_t*>(peer_bufs[j]);
+    }
+    return zipgemm_impl(stream, sm, full, b1, b2, b3, mt_off, gt_off, max_hf, max_full, start_exp, X, C, M, N, K, 1,
+                        err, &px);
 }
 
 }  // namespace zs

@@ -40,6 +40,21 @@ cudaError_t launch_zipgemm(cudaStream_t s, const uint8_t* sm, const uint16_t* fu
                            int max_hf, int max_full, int start_exp, const uint16_t* X, uint16_t* C, int M,
                            int N, int K, int split_k, unsigned* err);
 
+// Row-parallel ZipGEMM with the all-reduce of C over `world` GPUs fused into
+// its epilogue (see zs_zipgemm_allreduce).
+struct PeerExchange {
+    int world, rank;
+    uint16_t* recv[8];
+    unsigned* epoch;
+};
+size_t zipgemm_allreduce_counters(int M, int N);
+size_t zipgemm_allreduce_buffer_bytes(int M, int N, int world);
+cudaError_t launch_zipgemm_allreduce(cudaStream_t s, const uint8_t* sm, const uint16_t* full, const uint64_t* b1,
+                                     const uint64_t* b2, const uint64_t* b3, const int* mt_off, const int* gt_off,
+                                     int max_hf, int max_full, int start_exp, const uint16_t* X, uint16_t* C, int M,
+                                     int N, int K, int world, int rank, void* const* peer_bufs, unsigned* epoch,
+                                     unsigned* err);
+
 // One TCA-TBE compressed matrix (device pointers + scalars).
 struct AttnCompressed {
     const uint8_t* sm;

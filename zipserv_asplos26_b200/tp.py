@@ -38,6 +38,77 @@ def shard_cols(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     return w[:, rank * k:(rank + 1) * k].contiguous()
 
 
+class AllReduceBuffers:
+    """Exchange buffers of the fused row-parallel all-reduce (zs_zipgemm_allreduce)
+    for outputs of M x N: one buffer per rank in its own GPU memory, mapped
+    into every other rank through CUDA IPC (the handles travel over the
+    process group), plus this rank's per-tile exchange counters. Creating one
+    is collective over `group`; make it before any CUDA-graph capture."""
+
+    def __init__(self, M: int, N: int, group=None, device=None):
+        import ctypes as C
+        from ._lib import check, lib
+        self.rank, self.world = _rank_world(group)
+        if self.world < 2:
+            raise ValueError("the fused all-reduce needs at least 2 ranks")
+        L = lib()
+        self.M, self.N = M, N
+        nbytes = L.zs_zipgemm_allreduce_buffer_bytes(M, N, self.world)
+        if nbytes == 0:
+            raise ValueError(f"no exchange buffer for M={M} N={N} world={self.world}")
+        handle = C.create_string_buffer(L.zs_peer_handle_bytes())
+        own = C.c_void_p()
+        check(L.zs_peer_alloc(nbytes, C.byref(own), handle), "zs_peer_alloc")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._own = own.value
+        self._opened = []
+        ptrs = []
+        for j, h in enumerate(handles):
+            if j == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = C.c_void_p()
+            check(L.zs_peer_open(C.create_string_buffer(h, len(h)), C.byref(p)), "zs_peer_open")
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self.peer_array = (C.c_void_p * self.world)(*ptrs)
+        self.epoch = torch.zeros(L.zs_zipgemm_allreduce_counters(M, N), dtype=torch.int32, device=device)
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (after every rank's last call)."""
+        from ._lib import lib
+        L = lib()
+        for p in self._opened:
+            L.zs_peer_close(p)
+        self._opened = []
+        if self._own:
+            L.zs_peer_free(self._own)
+            self._own = None
+
+
+def zipgemm_allreduce(c, x: torch.Tensor, bufs: AllReduceBuffers, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y[N, M] = sum over ranks of x_r @ W_r^T, the all-reduce fused into the
+    ZipGEMM (zs_zipgemm_allreduce): `c` is this rank's compressed K shard of W,
+    `x` its [N, K_shard] slice of the activations. Every rank gets the same y."""
+    from ._lib import check, lib
+    from .codec import _check_2d_bf16
+    _check_2d_bf16(x, "x")
+    N, K = x.shape
+    if K != c.cols or (c.rows, N) != (bufs.M, bufs.N):
+        raise ValueError("x / W shard / exchange buffers disagree on M, N or K")
+    if out is None:
+        out = torch.empty(N, c.rows, dtype=torch.bfloat16, device=x.device)
+    _check_2d_bf16(out, "out")
+    check(lib().zs_zipgemm_allreduce(torch.cuda.current_stream().cuda_stream, c.sign_mantissa.data_ptr(),
+                                     c.compressed_full.data_ptr(), c.bitmap1.data_ptr(), c.bitmap2.data_ptr(),
+                                     c.bitmap3.data_ptr(), c.tile_offsets_median.data_ptr(),
+                                     c.tile_offsets_global.data_ptr(), c.max_high_freq_count, c.max_full_count,
+                                     c.start_exp, x.data_ptr(), out.data_ptr(), c.rows, N, K, bufs.world, bufs.rank,
+                                     bufs.peer_array, bufs.epoch.data_ptr(), None), "zs_zipgemm_allreduce")
+    return out
+
+
 def _zipgemm_backend(c, x, out=None):
     from .codec import zipgemm
     return zipgemm(c, x, out=out)
@@ -64,19 +135,32 @@ class ColumnParallelZipLinear:
 
 
 class RowParallelZipLinear:
-    """y[N, M] = sum over ranks of x_local[N, K/world] @ W_shard^T (all-reduce)."""
+    """y[N, M] = sum over ranks of x_local[N, K/world] @ W_shard^T (all-reduce).
+
+    fused=True (CUDA ranks): one zs_zipgemm_allreduce per call, the exchange
+    over NVLink inside the ZipGEMM; the exchange buffers for each token count
+    N are made on the first call with that N (collective: every rank calls
+    with the same N). fused=False: ZipGEMM, then torch.distributed.all_reduce
+    (any backend; the CPU tests use gloo)."""
 
     def __init__(self, w_shard: torch.Tensor, gemm: Callable = _zipgemm_backend,
-                 compressor: Callable = _compress_backend, group=None):
+                 compressor: Callable = _compress_backend, group=None, fused: bool = False):
         self.gemm = gemm
         self.group = group
+        self.fused = fused
         self.weight = compressor(w_shard)
         self.out_features = w_shard.shape[0]
         self.in_features = w_shard.shape[1]
+        self._bufs = {}
 
     def __call__(self, x_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        y = self.gemm(self.weight, x_local, out=out)
         _, world = _rank_world(self.group)
+        if self.fused and world > 1:
+            N = x_local.shape[0]
+            if N not in self._bufs:
+                self._bufs[N] = AllReduceBuffers(self.out_features, N, group=self.group, device=x_local.device)
+            return zipgemm_allreduce(self.weight, x_local, self._bufs[N], out=out)
+        y = self.gemm(self.weight, x_local, out=out)
         if world > 1:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         return y
@@ -89,12 +173,13 @@ LLAMA8B_SHAPES = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (28672, 409
 
 class TPLayerGemms:
     """The four weight GEMMs of one decoder layer, tensor-parallel:
-    QKV and gate_up column-parallel, O and down row-parallel (+ all-reduce).
+    QKV and gate_up column-parallel, O and down row-parallel (+ all-reduce,
+    fused into the ZipGEMM when fused=True).
     Weights are generated per rank from a seed (synthetic, N(0, sigma))."""
 
     def __init__(self, shapes=LLAMA70B_SHAPES, seed: int = 0, sigma: float = 0.02, device=None,
                  gemm: Callable = _zipgemm_backend, compressor: Callable = _compress_backend,
-                 dtype=torch.bfloat16, group=None):
+                 dtype=torch.bfloat16, group=None, fused: bool = False):
         rank, world = _rank_world(group)
         self.rank, self.world = rank, world
         self.layers = {}
@@ -107,8 +192,11 @@ class TPLayerGemms:
             g = torch.Generator(device=device if device is not None else "cpu")
             g.manual_seed(seed * 1000 + i * 16 + rank)
             w = (torch.randn(m, k, generator=g, device=device) * sigma).to(dtype)
-            cls = ColumnParallelZipLinear if col else RowParallelZipLinear
-            self.layers[name] = cls(w, gemm=gemm, compressor=compressor, group=group)
+            if col:
+                self.layers[name] = ColumnParallelZipLinear(w, gemm=gemm, compressor=compressor, group=group)
+            else:
+                self.layers[name] = RowParallelZipLinear(w, gemm=gemm, compressor=compressor, group=group,
+                                                         fused=fused)
 
     def input_shapes(self, n_tokens: int):
         """Activation shapes each projection consumes on this rank."""
