@@ -12,7 +12,10 @@ ranks' rows once they have landed); `unfused_nccl_us_per_step` times the same
 steps as ZipGEMM + NCCL all-reduce, as context. The timed region
 is K CUDA-graph replayed steps bracketed by barrier + synchronize; time = max
 over ranks. Before the headline line, the config-4 Llama-70B layer at tp = N
-is printed (one line per token count).
+is printed (one line per token count); at N = 1 the other BASELINE
+configurations are printed first as well (config 1 round trip, config 3
+Llama-8B projections against cuBLAS, config 5 decode attention against stock
+flash-attn), unless --headline-only is given.
 
 L2 policy: each rank rotates through enough distinct compressed weights that
 the rotating set exceeds the 126 MB L2, so every step streams its weight from
@@ -659,6 +662,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="N = 1: skip the config 1 / 3 / 5 lines printed before the headline")
     ap.add_argument("--ncu", action="store_true", help="plain launches for ncu, no timing")
     ap.add_argument("--weight-offload", action="store_true",
                     help="with --workload llama8b: copy the weight H2D inside every timed step")
@@ -682,6 +687,13 @@ def main():
 
     lib()
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world == 1 and not args.headline_only:
+        # the other BASELINE configurations, one JSON line per case, before the headline
+        import torch as _t
+        for run in (run_roundtrip, run_llama8b, run_attention):
+            run(args)
+            _t.cuda.synchronize()
+            _t.cuda.empty_cache()
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)

@@ -42,6 +42,37 @@ __device__ __forceinline__ uint32_t st_order_inclusive_scan(uint32_t v, int lane
     return __shfl_sync(0xFFFFFFFFu, x, (lane & 16) | s);
 }
 
+// Overwrite one lane's fallback elements (code 0) in place. Bit j of fm
+// (j = 8 * row + column, rows relative to row0) marks a fallback; its value is
+// the next element of the fallback stream from element f on (clamped to
+// full_cap). Values are fetched kFbBatch at a time with independent loads, so
+// their shared-memory latencies overlap, and then stored; the loop runs until
+// the lane with the most fallbacks is done.
+#ifndef ZS_FB_BATCH
+#define ZS_FB_BATCH 2
+#endif
+constexpr int kFbBatch = ZS_FB_BATCH;
+__device__ __forceinline__ void patch_fallbacks(uint32_t fm, uint32_t f, uint32_t full, uint32_t full_cap,
+                                                uint32_t row0, uint32_t sw) {
+    while (fm) {
+        uint32_t pos[kFbBatch], val[kFbBatch];
+#pragma unroll
+        for (int k = 0; k < kFbBatch; ++k) {
+            pos[k] = (uint32_t)__ffs(fm) - 1u;   // all ones once fm is empty
+            fm &= fm - 1u;
+            val[k] = lds16(full + 2u * min(f + (uint32_t)k, full_cap));
+        }
+#pragma unroll
+        for (int k = 0; k < kFbBatch; ++k) {
+            if (pos[k] < 32u) {
+                const uint32_t r = pos[k] >> 3, c = pos[k] & 7u;
+                sts16(row0 + 128u * r + ((sw ^ r) << 4) + 2u * c, val[k]);
+            }
+        }
+        f += kFbBatch;
+    }
+}
+
 // Decode median tile w (16 rows x 64 columns = 16 small tiles) of a staged GT
 // into 16 consecutive rows of a 128-byte-row bf16 tile in the UMMA canonical
 // 128-byte-swizzle layout (16-byte chunk c of tile row m at (c ^ (m & 7)) * 16).
@@ -83,15 +114,7 @@ __device__ __forceinline__ void decode_mt_to_tile(const GtView& g, const DecodeT
         decode_row_words(w1, w2, w3, (uint32_t)r, g.sm + hf, t, o);
         sts128(base + 128u * (uint32_t)r + ((sw ^ (uint32_t)r) << 4), o[0], o[1], o[2], o[3]);
     }
-    uint32_t fm = ~ind;
-    uint32_t f = fs;
-    while (fm) {
-        const uint32_t j = __ffs(fm) - 1;
-        fm &= fm - 1;
-        const uint32_t r = j >> 3, c = j & 7;
-        sts16(base + 128u * r + ((sw ^ r) << 4) + 2u * c, lds16(g.full + 2u * min(f, g.full_cap)));
-        ++f;
-    }
+    patch_fallbacks(~ind, fs, g.full, g.full_cap, base, sw);
 }
 
 // Decode median tiles w0 and w0 + 1 of a staged GT (32 consecutive rows) into
@@ -138,17 +161,8 @@ __device__ __forceinline__ void decode_mt2_to_tile(const GtView& g, const Decode
             sts128(b0 + 2048u * (uint32_t)q + 128u * (uint32_t)r + ((sw ^ (uint32_t)r) << 4), o[0], o[1], o[2], o[3]);
         }
     }
-    uint32_t fm0 = ~IND[0], fm1 = ~IND[1];
-    uint32_t f0 = FS[0], f1 = FS[1];
-    while (fm0 | fm1) {
-        const bool a = fm0 != 0;
-        const uint32_t fm = a ? fm0 : fm1;
-        const uint32_t j = __ffs(fm) - 1;
-        const uint32_t r = j >> 3, c = j & 7;
-        const uint32_t f = a ? f0 : f1;
-        sts16(b0 + (a ? 0u : 2048u) + 128u * r + ((sw ^ r) << 4) + 2u * c, lds16(g.full + 2u * min(f, g.full_cap)));
-        if (a) { fm0 &= fm0 - 1; ++f0; } else { fm1 &= fm1 - 1; ++f1; }
-    }
+    patch_fallbacks(~IND[0], FS[0], g.full, g.full_cap, b0, sw);
+    patch_fallbacks(~IND[1], FS[1], g.full, g.full_cap, b0 + 2048u, sw);
 }
 
 // Shared-memory footprint helpers for one staged GT.
