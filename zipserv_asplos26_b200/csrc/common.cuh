@@ -446,25 +446,40 @@ __device__ __forceinline__ uint32_t lop_or_and(uint32_t a, uint32_t mask, uint32
     return (a & mask) | b;  // compiles to a single LOP3
 }
 
-// Decode the high-frequency elements of one small-tile row (8 elements) from
-// the three bitmap words of a small tile's row half (w1, w2, w3: rows 4h ..
-// 4h+3, one byte per row), row r (0..3) of them; fallback positions (code 0)
+// Bit groups of the three bitmap words of a small tile's row half (w1, w2, w3:
+// rows 4h .. 4h+3, one byte per row): for each bitmap, a holds groups 0 and 1
+// (bits 0-1 and 2-3) of row r's byte as the two nibbles of byte r, and b
+// groups 2 and 3 (bits 4-5 and 6-7). Five logic/shift ops per bitmap serve
+// all four rows.
+struct RowGroups {
+    uint32_t a1, b1, a2, b2, a3, b3;
+};
+__device__ __forceinline__ void bit_groups(uint32_t w, uint32_t& a, uint32_t& b) {
+    a = (w & 0x03030303u) | ((w << 2) & 0x30303030u);
+    b = ((w >> 4) & 0x03030303u) | ((w >> 2) & 0x30303030u);
+}
+__device__ __forceinline__ RowGroups row_groups(uint32_t w1, uint32_t w2, uint32_t w3) {
+    RowGroups g;
+    bit_groups(w1, g.a1, g.b1);
+    bit_groups(w2, g.a2, g.b2);
+    bit_groups(w3, g.a3, g.b3);
+    return g;
+}
+
+// Decode the high-frequency elements of one small-tile row (8 elements), row r
+// (0..3) of the row half whose bit groups are g; fallback positions (code 0)
 // receive junk that the caller patches. The spread of a bitmap byte c (nibble
 // j = bit j) has byte k = {0x00, 0x01, 0x10, 0x11}[(c >> 2k) & 3], so one
 // byte permute of the constant 0x11100100 produces it from a selector whose
-// nibble k is bit group k of c; the selectors of bitmaps 1 and 2 are built
-// together in one word.
-__device__ __forceinline__ uint32_t bit_group_selectors(uint32_t x) {   // x: one byte in bytes 0 and/or 2
-    x = (x | (x << 4)) & 0x0F0F0F0Fu;
-    return (x | (x << 2)) & 0x33333333u;
-}
-__device__ __forceinline__ void decode_row_words(uint32_t w1, uint32_t w2, uint32_t w3, uint32_t r, uint32_t win,
-                                                 const DecodeTables& t, uint32_t (&o)[4]) {
+// nibble k is bit group k of c; a second byte permute gathers that selector
+// (bytes r of a and b) from the row half's bit groups.
+__device__ __forceinline__ void decode_row_words(const RowGroups& g, uint32_t r, uint32_t win, const DecodeTables& t,
+                                                 uint32_t (&o)[4]) {
     constexpr uint32_t kSpreadBytes = 0x11100100u;
-    const uint32_t g12 = bit_group_selectors(prmt(w1, w2, r | ((4u + r) << 8)) & 0x00FF00FFu);
-    const uint32_t g3 = bit_group_selectors(prmt(w3, 0, 0x4440u | r));
-    const uint32_t s1 = prmt(kSpreadBytes, 0, g12), s2 = prmt(kSpreadBytes, 0, g12 >> 16),
-                   s3 = prmt(kSpreadBytes, 0, g3);
+    const uint32_t gsel = r | ((4u + r) << 4);
+    const uint32_t s1 = prmt(kSpreadBytes, 0, prmt(g.a1, g.b1, gsel)),
+                   s2 = prmt(kSpreadBytes, 0, prmt(g.a2, g.b2, gsel)),
+                   s3 = prmt(kSpreadBytes, 0, prmt(g.a3, g.b3, gsel));
     const uint32_t X = s1 + (s2 << 1) + (s3 << 2);        // code nibbles
     const uint32_t sel = (s1 | s2 | s3) * 0x11111110u;    // hf-before-j nibbles
     const uint32_t wa = win & ~3u;

@@ -106,12 +106,13 @@ __device__ __forceinline__ void decode_mt_to_tile(const GtView& g, const DecodeT
     const uint32_t w1 = rh ? v1.y : v1.x, w2 = rh ? v2.y : v2.x, w3 = rh ? v3.y : v3.x;
     const uint32_t base = rows + 128u * (8u * (uint32_t)mr + 4u * (uint32_t)rh);
     const uint32_t sw = (uint32_t)kc ^ (4u * (uint32_t)rh);   // swizzled chunk of row r is sw ^ r
+    const RowGroups rg = row_groups(w1, w2, w3);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         const uint32_t pre = r ? (uint32_t)__popc(ind & ((1u << (8 * r)) - 1u)) : 0u;
         const uint32_t hf = min(hs + pre, g.hf_cap);
         uint32_t o[4];
-        decode_row_words(w1, w2, w3, (uint32_t)r, g.sm + hf, t, o);
+        decode_row_words(rg, (uint32_t)r, g.sm + hf, t, o);
         sts128(base + 128u * (uint32_t)r + ((sw ^ (uint32_t)r) << 4), o[0], o[1], o[2], o[3]);
     }
     patch_fallbacks(~ind, fs, g.full, g.full_cap, base, sw);
@@ -152,12 +153,13 @@ __device__ __forceinline__ void decode_mt2_to_tile(const GtView& g, const Decode
     const uint32_t b0 = rows + 128u * (8u * (uint32_t)mr + 4u * (uint32_t)rh);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
+        const RowGroups rg = row_groups(W1[q], W2[q], W3[q]);
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const uint32_t pre = r ? (uint32_t)__popc(IND[q] & ((1u << (8 * r)) - 1u)) : 0u;
             const uint32_t hf = min(HS[q] + pre, g.hf_cap);
             uint32_t o[4];
-            decode_row_words(W1[q], W2[q], W3[q], (uint32_t)r, g.sm + hf, t, o);
+            decode_row_words(rg, (uint32_t)r, g.sm + hf, t, o);
             sts128(b0 + 2048u * (uint32_t)q + 128u * (uint32_t)r + ((sw ^ (uint32_t)r) << 4), o[0], o[1], o[2], o[3]);
         }
     }
