@@ -1,5 +1,7 @@
 """Row-parallel ZipGEMM with the all-reduce fused into the kernel
-(zs_zipgemm_allreduce), one process per GPU, world sizes 2..device count.
+(zs_zipgemm_allreduce), one process per GPU, world sizes 2..device count,
+with both exchange schemes (all-to-all, and reduce-scatter + all-gather by
+tile owner).
 
 The expected output is exact: every rank's partial is its own ZipGEMM of its
 K shard (zs_zipgemm, bf16), and the fused kernel must return, on every rank,
@@ -108,10 +110,17 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_gpu_zipgemm_allreduce_matches_partials(world):
+@pytest.mark.parametrize("world,scheme", [(2, None), (2, "owner"), (4, None), (4, "all2all"), (8, None)])
+def test_gpu_zipgemm_allreduce_matches_partials(world, scheme, monkeypatch):
+    """scheme None: the default exchange for the world size (all-to-all at 2
+    ranks, reduce-scatter + all-gather by tile owner from 3 on); "owner" /
+    "all2all" force the other one through ZS_ALLREDUCE_SCHEME."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
+    if scheme:
+        monkeypatch.setenv("ZS_ALLREDUCE_SCHEME", scheme)
+    else:
+        monkeypatch.delenv("ZS_ALLREDUCE_SCHEME", raising=False)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()

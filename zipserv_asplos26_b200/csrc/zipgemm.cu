@@ -50,6 +50,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "tile_decode.cuh"
@@ -106,6 +107,7 @@ struct GemmParams {
     // each tile has completed. Column chunk n0 of Ntot; flag_base offsets the
     // chunk's counters.
     int world, rank, Ntot, n0, flag_base;
+    int ar_owned;   // 1: reduce-scatter + all-gather by tile owner, 0: all-to-all
     uint16_t* recv[8];
     unsigned* epoch;
     int debug;   // diagnostic builds only (-DZS_TRACE): experiment bits
@@ -202,17 +204,47 @@ __device__ __forceinline__ void cluster_reduce(const GemmParams& p, uint32_t par
 // The split-tile sum fused with the row-parallel all-reduce over `world` GPUs.
 // CTA r of the cluster sums its rows of the S partial tiles (as cluster_reduce)
 // and rounds this rank's result to bf16 (what an all-reduce of the bf16
-// partial Ys would receive). Each 8-byte word it sends holds two bf16 values
-// and the tile's exchange number (flag = exchanges completed + 1), so a word
-// is complete the moment it is visible: it stores its words into slot `rank`
-// of every peer's exchange buffer over NVLink, then polls the peers' words in
-// its own buffer until their flags match (bounded), and adds the `world`
-// partials in rank order in fp32 before writing bf16 C, so every rank
-// computes bit-identical Y. No fence, counter or barrier is needed. The
-// buffer has two halves, chosen by the parity of the exchange number: a rank
-// can be one exchange ahead of a peer that is still reading, never two (its
-// next exchange needs that peer's next words, which the peer stores only
-// after it has read this exchange's).
+// partial Ys would receive). Each 8-byte word sent over NVLink holds two bf16
+// values and the tile's exchange number (flag = exchanges completed + 1), so a
+// word is complete the moment it is visible; a thread stores two words (four
+// rows of one column) with one 16-byte store, so a warp writes whole 128-byte
+// lines. The `world` partials are added in rank order in fp32, so every rank
+// ends with bit-identical Y. No fence, counter or barrier crosses the GPUs.
+//   all-to-all (the default for world == 2). Each rank stores its partial into slot `rank` of
+//     the peer's exchange buffer, waits for the peer's words in its own, and
+//     sums (2 MiB of words per MiB of Y leave each GPU).
+//   by tile owner (the default for world >= 3): reduce-scatter + all-gather. Tile T belongs
+//     to rank T % world. The other ranks store their partial rows of T into
+//     the owner's buffer (slot = their rank); the owner sums them, writes C and
+//     stores the final bf16 rows into slot `owner` of every other rank's
+//     buffer, where the other ranks wait for them. Each GPU sends
+//     2 (world - 1) / world words per value instead of world - 1.
+// The buffer has two halves, chosen by the parity of the exchange number: a
+// rank can be one exchange ahead of a peer that is still reading, never two
+// (its next exchange of a tile needs that peer's words of this one, which the
+// peer stores only after it has read this exchange's).
+__device__ __forceinline__ void st_volatile_v2u64(unsigned long long* p, unsigned long long a, unsigned long long b) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void ld_volatile_v2u64(const unsigned long long* p, unsigned long long& a,
+                                                  unsigned long long& b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+// Wait (bounded) until both words at src carry `flag`; returns their payloads.
+__device__ __forceinline__ uint2 wait_words(const unsigned long long* src, unsigned long long flag, bool& ok,
+                                            long long t0, unsigned* err) {
+    unsigned long long w0 = 0, w1 = 0;
+    for (uint32_t it = 0;; ++it) {
+        ld_volatile_v2u64(src, w0, w1);
+        if ((w0 & 0xFFFFFFFF00000000ull) == flag && (w1 & 0xFFFFFFFF00000000ull) == flag) break;
+        if (!ok || ((it & 255) == 255 && clock64() - t0 > kWaitLimitCycles)) {
+            if (ok && err) atomicOr(err, kErrWaitTimeout);
+            ok = false;
+            break;
+        }
+    }
+    return make_uint2((uint32_t)w0, (uint32_t)w1);
+}
 constexpr int kArMaxItems = 8;   // items (4 rows x 1 column) per thread: BN * 32 / S / kGemmThreads <= 7
 template <int S>
 __device__ __forceinline__ void cluster_reduce_allreduce(const GemmParams& p, uint32_t part, int T, int r, int tid) {
@@ -223,6 +255,8 @@ __device__ __forceinline__ void cluster_reduce_allreduce(const GemmParams& p, ui
     const unsigned long long flag = (unsigned long long)(cnt + 1u) << 32;
     const size_t slot = (size_t)p.Ntot * (size_t)p.M / 2;   // 8-byte words of one rank's partial
     const size_t half = (size_t)(cnt & 1u) * (size_t)p.world * slot;
+    const bool owned = p.ar_owned != 0;
+    const int owner = owned ? T % p.world : p.rank;   // the rank that sums this tile
     uint2 own[kArMaxItems];
 #pragma unroll
     for (int t = 0; t < kArMaxItems; ++t) {
@@ -245,10 +279,9 @@ __device__ __forceinline__ void cluster_reduce_allreduce(const GemmParams& p, ui
         if (col < p.N && m < p.M) {
             const size_t off = half + (size_t)p.rank * slot + ((size_t)(p.n0 + col) * p.M + m) / 2;
             for (int j = 0; j < p.world; ++j) {
-                if (j == p.rank) continue;
-                volatile unsigned long long* dst = reinterpret_cast<unsigned long long*>(p.recv[j]) + off;
-                dst[0] = flag | own[t].x;
-                dst[1] = flag | own[t].y;
+                if (j == p.rank || (owned && j != owner)) continue;
+                st_volatile_v2u64(reinterpret_cast<unsigned long long*>(p.recv[j]) + off, flag | own[t].x,
+                                  flag | own[t].y);
             }
         }
     }
@@ -261,38 +294,34 @@ __device__ __forceinline__ void cluster_reduce_allreduce(const GemmParams& p, ui
         const int col = e / R4, m4 = R * r + 4 * (e - col * R4);
         const int m = 128 * T + m4;
         if (col >= p.N || m >= p.M) continue;
-        const volatile unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.recv[p.rank]) + half +
-                                                 ((size_t)(p.n0 + col) * p.M + m) / 2;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j = 0; j < p.world; ++j) {
-            uint2 q = own[t];
-            if (j != p.rank) {
-                unsigned long long w0, w1;
-                for (uint32_t it = 0;; ++it) {
-                    w0 = src[(size_t)j * slot];
-                    w1 = src[(size_t)j * slot + 1];
-                    if ((w0 & 0xFFFFFFFF00000000ull) == flag && (w1 & 0xFFFFFFFF00000000ull) == flag) break;
-                    if (!ok || ((it & 255) == 255 && clock64() - t0 > kWaitLimitCycles)) {
-                        if (ok && p.err) atomicOr(p.err, kErrWaitTimeout);
-                        ok = false;
-                        break;
-                    }
-                }
-                q.x = (uint32_t)w0;
-                q.y = (uint32_t)w1;
-            }
-            const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
-            const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
-            if (j == 0) {
-                acc = make_float4(lo.x, lo.y, hi.x, hi.y);
-            } else {
-                acc.x += lo.x; acc.y += lo.y; acc.z += hi.x; acc.w += hi.y;
-            }
-        }
-        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+        const size_t word = ((size_t)(p.n0 + col) * p.M + m) / 2;
+        const unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.recv[p.rank]) + half + word;
         uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&lo);
-        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        if (p.rank == owner) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j < p.world; ++j) {
+                const uint2 q = j == p.rank ? own[t] : wait_words(src + (size_t)j * slot, flag, ok, t0, p.err);
+                const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
+                const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
+                if (j == 0) {
+                    acc = make_float4(lo.x, lo.y, hi.x, hi.y);
+                } else {
+                    acc.x += lo.x; acc.y += lo.y; acc.z += hi.x; acc.w += hi.y;
+                }
+            }
+            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+            pk.x = *reinterpret_cast<uint32_t*>(&lo);
+            pk.y = *reinterpret_cast<uint32_t*>(&hi);
+            if (owned) {   // all-gather: the final rows to every other rank (slot `owner`)
+                const size_t off = half + (size_t)p.rank * slot + word;
+                for (int j = 0; j < p.world; ++j)
+                    if (j != p.rank)
+                        st_volatile_v2u64(reinterpret_cast<unsigned long long*>(p.recv[j]) + off, flag | pk.x,
+                                          flag | pk.y);
+            }
+        } else {
+            pk = wait_words(src + (size_t)owner * slot, flag, ok, t0, p.err);
+        }
         *reinterpret_cast<uint2*>(p.C + (size_t)col * p.M + m) = pk;
     }
     if (tid == 0) p.epoch[fidx] = cnt + 1u;
@@ -854,6 +883,12 @@ static cudaError_t zipgemm_impl(cudaStream_t stream, const uint8_t* sm, const ui
         p.rank = px->rank;
         p.Ntot = N;
         p.epoch = px->epoch;
+        // ZS_ALLREDUCE_SCHEME=owner|all2all overrides the default, to compare the two
+        static const int forced = [] {
+            const char* e = getenv("ZS_ALLREDUCE_SCHEME");
+            return !e ? -1 : (std::string(e) == "owner" ? 1 : (std::string(e) == "all2all" ? 0 : -1));
+        }();
+        p.ar_owned = forced >= 0 ? forced : (px->world >= 3 ? 1 : 0);
         for (int j = 0; j < px->world; ++j) p.recv[j] = px->recv[j];
     }
     // N > 256 runs as column chunks of 256 (each re-decodes W; such N are
