@@ -22,6 +22,7 @@
 #include <mutex>
 #include <cmath>
 #include <cstddef>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "tile_decode.cuh"
@@ -39,8 +40,8 @@ constexpr int kAttnProducer = 16;
 constexpr int kAttnMath0 = 17;      // math warps 17 and 18 take alternate pages
 constexpr int kAttnWarps = 19;
 constexpr int kAttnThreads = 32 * kAttnWarps;
-constexpr int kAttnSlots = 3;       // compressed pages (K + V) in flight
-constexpr int kAttnTiles = 3;       // decoded pages: K 16 KB + V 16 KB each
+constexpr int kAttnSlots = 4;       // compressed pages (K + V) in flight (ring depth up to 4)
+constexpr int kAttnTiles = 3;       // decoded pages: K 16 KB + V 16 KB each (ring depth up to 3)
 constexpr uint32_t kAttnTileBytes = 32768;
 
 struct AttnStream {
@@ -67,7 +68,8 @@ struct AttnParams {
     //   [b1 | b2 | b3: 2 GTs x 512 B each] [mt: 2 x 32 B] [hf: 2 GTs] [fallback: 2 GTs]
     uint32_t c_mat, c_hf, c_full, hf_cap, full_cap, c_slot;
     uint32_t off_tiles, off_slots;
-    int nslots;               // depth of the page rings (compressed slots and decoded tiles): 3, or 2 for large streams
+    int nslots;               // depth of the compressed page ring (attn_rings)
+    int ntiles;               // depth of the decoded tile ring (attn_rings)
     unsigned* err;
     // Paged layout (block_table != nullptr): logical page g of sequence b is
     // physical page block_table[b * max_blocks + g] * Hkv + kv head; when the
@@ -87,17 +89,31 @@ struct AttnParams {
     const unsigned long long* k_max;
     const unsigned long long* v_max;
     uint32_t smem_bytes;
+    int ring_pref;            // first candidate of attn_rings to try
 };
 
 // Shared-memory carve-up of the page rings (from the host, or from the pools'
 // device-side maxima in the paged layout).
 struct AttnLayout {
     uint32_t c_hf, hf_cap, c_full, full_cap, c_mat, c_slot, off_slots;
-    int nslots;
+    int nslots, ntiles;
 };
 
+// Depths of the compressed-page ring and the decoded-tile ring: the first
+// candidate (from `pref` on) whose rings fit in `smem` bytes after the
+// `off_tiles` header; (2, 2) always fits the largest streams.
+__host__ __device__ inline void attn_rings(uint32_t off_tiles, uint32_t c_slot, uint32_t smem, int pref, int& nc,
+                                           int& nt) {
+    const int cand[3][2] = {{4, 3}, {3, 3}, {2, 2}};
+    for (int i = pref < 0 ? 0 : (pref > 2 ? 2 : pref); i < 3; ++i) {
+        nc = cand[i][0];
+        nt = cand[i][1];
+        if (off_tiles + (uint32_t)nt * kAttnTileBytes + (uint32_t)nc * c_slot <= smem) return;
+    }
+}
+
 __device__ __forceinline__ AttnLayout attn_layout(const AttnParams& p) {
-    AttnLayout L{p.c_hf, p.hf_cap, p.c_full, p.full_cap, p.c_mat, p.c_slot, p.off_slots, p.nslots};
+    AttnLayout L{p.c_hf, p.hf_cap, p.c_full, p.full_cap, p.c_mat, p.c_slot, p.off_slots, p.nslots, p.ntiles};
     if (p.k_max) {
         const unsigned long long mh = max(p.k_max[0], p.v_max[0]), mf = max(p.k_max[1], p.v_max[1]);
         const uint32_t hfc = (uint32_t)min(mh, 4096ull + 16), ffc = (uint32_t)min(mf, 4096ull + 8) * 2u;
@@ -106,8 +122,8 @@ __device__ __forceinline__ AttnLayout attn_layout(const AttnParams& p) {
         L.full_cap = 2u * ((ffc + 15u) & ~15u);
         L.c_mat = (L.c_full + L.full_cap + 16u + 127u) & ~127u;
         L.c_slot = 2u * L.c_mat;
-        L.nslots = p.off_tiles + 3u * (kAttnTileBytes + L.c_slot) <= p.smem_bytes ? 3 : 2;
-        L.off_slots = p.off_tiles + (uint32_t)L.nslots * kAttnTileBytes;
+        attn_rings(p.off_tiles, L.c_slot, p.smem_bytes, p.ring_pref, L.nslots, L.ntiles);
+        L.off_slots = p.off_tiles + (uint32_t)L.ntiles * kAttnTileBytes;
     }
     return L;
 }
@@ -195,6 +211,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
         for (int s = 0; s < L.nslots; ++s) {
             mbar_init(&A.cfull[s], 1);
             mbar_init(&A.cempty[s], kAttnDecWarps);
+        }
+        for (int s = 0; s < L.ntiles; ++s) {
             mbar_init(&A.tfull[s], kAttnDecWarps);
             mbar_init(&A.tempty[s], 1);
         }
@@ -287,12 +305,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
     } else if (warp < kAttnDecWarps) {
         const int mat = warp >> 3, gc = (warp >> 2) & 1, mtile = warp & 3;
         const DecodeTables tabs = make_decode_tables(mat ? p.v.start_exp : p.k.start_exp);
-        int s = 0;
-        uint32_t ph = 0;
+        int s = 0, t = 0;   // compressed slot, tile slot
+        uint32_t ph = 0, tph = 0;
         for (int pi = 0; pi < np; ++pi) {
             if (*abort_flag) break;
             if (!mbar_wait_sleep(&A.cfull[s], ph, p.err, abort_flag)) break;
-            if (pi >= L.nslots && !mbar_wait_sleep(&A.tempty[s], ph ^ 1u, p.err, abort_flag)) break;
+            if (pi >= L.ntiles && !mbar_wait_sleep(&A.tempty[t], tph ^ 1u, p.err, abort_flag)) break;
             const uint32_t base = launder(smem0 + L.off_slots + (uint32_t)s * L.c_slot + (uint32_t)mat * L.c_mat);
             const int2 inf = gc ? A.info[s][mat] : make_int2(0, 0);
             const uint32_t h0 = min((uint32_t)inf.x, L.hf_cap), f0 = min((uint32_t)inf.y, L.full_cap / 2);
@@ -304,7 +322,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             g.full = base + L.c_full + 2u * f0;
             g.hf_cap = L.hf_cap - h0;
             g.full_cap = L.full_cap / 2 - f0;
-            const uint32_t rows = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes + 16384u * (uint32_t)mat +
+            const uint32_t rows = smem0 + p.off_tiles + (uint32_t)t * kAttnTileBytes + 16384u * (uint32_t)mat +
                                   8192u * (uint32_t)gc + 2048u * (uint32_t)mtile;
             if (is_dense_page(pg0 + pi)) {
                 // dense page (a paged sequence's tail, or every page in dense mode):
@@ -327,10 +345,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             }
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&A.tfull[s]);
+                mbar_arrive(&A.tfull[t]);
                 mbar_arrive(&A.cempty[s]);
             }
             if (++s == L.nslots) { s = 0; ph ^= 1u; }
+            if (++t == L.ntiles) { t = 0; tph ^= 1u; }
         }
     } else {
         // Math warps, one page each in turn. The m16n8k16 tiles put the page's
@@ -353,7 +372,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
         float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
         const int lr = (lane & 7) + 8 * ((lane >> 3) & 1), lc = lane >> 4;   // ldmatrix row / 8-column half (K)
         const int vr = (lane & 7) + 8 * (lane >> 4), vc = (lane >> 3) & 1;    // ldmatrix.trans token / dim half (V)
-        int s = mw % L.nslots, kround = mw / L.nslots;   // page pi = mw + 2j: tile slot pi % n, round pi / n
+        int s = mw % L.ntiles, kround = mw / L.ntiles;   // page pi = mw + 2j: tile slot pi % n, round pi / n
         for (int pi = mw; pi < np; pi += 2) {
             if (!mbar_wait(&A.tfull[s], (uint32_t)(kround & 1), p.err, abort_flag)) break;
             const uint32_t kt = smem0 + p.off_tiles + (uint32_t)s * kAttnTileBytes, vt = kt + 16384u;
@@ -443,7 +462,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
             __syncwarp();
             if (lane == 0) mbar_arrive(&A.tempty[s]);
             s += 2;
-            while (s >= L.nslots) { s -= L.nslots; ++kround; }
+            while (s >= L.ntiles) { s -= L.ntiles; ++kround; }
         }
         // merge the two math warps: warp kAttnMath0 + 1 publishes, kAttnMath0 combines and writes
         if (mw == 1) {
@@ -534,6 +553,16 @@ size_t attn_workspace_bytes(int B, int Hq, int Hkv, int num_splits) {
 // 2 standing for a CTA's set-up and its share of the combine. (A count that
 // only targeted about two CTAs per SM left 320 CTAs = 2.2 waves at B = 8,
 // T = 32768: a last wave 16% full.)
+// First ring candidate to try (attn_rings): 0 unless ZS_ATTN_RING in the
+// environment names another, to compare ring depths on the same build.
+static int attn_ring_pref() {
+    static const int v = [] {
+        const char* e = std::getenv("ZS_ATTN_RING");
+        return e ? std::atoi(e) : 0;
+    }();
+    return v;
+}
+
 int attn_default_splits(int B, int Hkv, int max_pages) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -631,12 +660,13 @@ static cudaError_t attention_core(cudaStream_t stream, const AttnCompressed& kc,
     int dev = 0, max_smem = 232448;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    // three pages in flight when the streams allow (large fallback streams, e.g.
-    // zero-padded pages, leave room for two)
-    p.nslots = 3;
-    while (p.nslots > 2 && p.off_tiles + (uint32_t)p.nslots * (kAttnTileBytes + p.c_slot) > (uint32_t)max_smem)
-        --p.nslots;
-    p.off_slots = p.off_tiles + (uint32_t)p.nslots * kAttnTileBytes;
+    // four compressed pages and three decoded tiles when the streams allow (the
+    // compressed ring hides the HBM latency of a page's copies; a fourth slot
+    // measured 3% faster at B=8, T=32768, a fourth tile nothing); large fallback
+    // streams (e.g. zero-padded pages) leave room for two of each
+    p.ring_pref = attn_ring_pref();
+    attn_rings(p.off_tiles, p.c_slot, (uint32_t)max_smem, p.ring_pref, p.nslots, p.ntiles);
+    p.off_slots = p.off_tiles + (uint32_t)p.ntiles * kAttnTileBytes;
     uint32_t smem_bytes = p.off_slots + (uint32_t)p.nslots * p.c_slot;
     if (smem_bytes > (uint32_t)max_smem) return cudaErrorInvalidValue;
     // with the pools' device-side maxima the kernel sizes its own page slots
