@@ -85,10 +85,14 @@ int zs_zipgemm(void* stream, const uint8_t* d_sm, const uint16_t* d_full, const 
  * Every rank calls it with its own compressed K shard of W (M x K), its K
  * slice of X (N x K) and the same M and N; on return d_c holds, on every rank,
  * bf16(sum over ranks j in order 0..world-1 of bf16(W_j X_j^T)), bit-identical
- * across ranks. Each CTA stores its finished rows over NVLink into every
- * peer's exchange buffer, as 8-byte words of two bf16 values and the call's
- * flag, and polls (bounded, about 2 s; then error bit 1 in *d_err) its own
- * buffer until the peers' words of the same rows carry the flag.
+ * across ranks. Words cross NVLink as 8-byte (two bf16 values, the call's
+ * flag) pairs in 16-byte stores, and a CTA polls (bounded, about 2 s; then
+ * error bit 1 in *d_err) its own buffer until the words it needs carry the
+ * flag. With 2 ranks each CTA stores its rows into the peer's buffer and sums
+ * both; from 3 ranks on, output tile t (128 rows) is summed by rank t % world,
+ * which receives the other ranks' rows of it and stores the final rows back
+ * into theirs (environment ZS_ALLREDUCE_SCHEME=all2all|owner overrides the
+ * choice; every rank must see the same value).
  *
  * peer_bufs: host array of `world` device pointers: rank j's exchange buffer
  * of zs_zipgemm_allreduce_buffer_bytes(M, N, world) bytes, zeroed, opened on
