@@ -178,6 +178,18 @@ def test_gpu_zipgemm_stream_k_segments(zs, oracle, M, K, N):
     _gemm_check(zs, oracle, M, K, N, seed=M + N)
 
 
+@pytest.mark.parametrize("mode", ["1", "0"])
+@pytest.mark.parametrize("M,K,N", [(4096, 4096, 128), (28672, 4096, 16), (57344, 1024, 300), (8256, 192, 7),
+                                   (20032, 320, 40)])
+def test_gpu_zipgemm_persistent_mode(zs, oracle, monkeypatch, mode, M, K, N):
+    """Persistent launch (one CTA per SM looping over tiles, two TMEM
+    accumulators, epilogue warps) forced on (1) and off (0): several tiles per
+    CTA, a half tile (M % 128 = 64) among them, odd K-block counts (one-unit
+    chunks), N > 256 (two column chunks)."""
+    monkeypatch.setenv("ZS_ZIPGEMM_PERSIST", mode)
+    _gemm_check(zs, oracle, M, K, N, seed=M + K + N)
+
+
 def test_gpu_zipgemm_deterministic(zs):
     """The split-tile reduction sums partials in a fixed order: repeated runs
     are bit-identical."""

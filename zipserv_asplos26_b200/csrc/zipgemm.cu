@@ -90,6 +90,7 @@ struct GemmParams {
     int gtk, mgt;                   // K blocks per GT row, GT rows
     int BN, xrows;                  // accumulator columns; rows of the X box = min(BN, N)
     int S;                          // CTAs per cluster (K split)
+    int tiles;                      // output tiles (128 rows) of the launch
     int cu, nc, na, nb;             // units per compressed chunk; ring depths
     uint32_t off_offs;              // staged GT offsets: [2 GT rows][nmax + 1] int2 (hf, fallback) unit boundaries
     int nmax;                       // most units of any CTA
@@ -125,6 +126,7 @@ struct GemmHeader {
     uint64_t a_full[kMaxRing], a_empty[kMaxRing];
     uint64_t b_full[kMaxRing], b_empty[kMaxRing];
     uint64_t acc_full;
+    uint64_t acc_full_p[2], acc_empty_p[2];   // persistent mode: the two TMEM accumulators
     uint32_t tmem_base;
     int abort_flag;
     int ctag[kMaxRing];   // newest chunk issued into each compressed slot (-1: none)
@@ -327,30 +329,47 @@ __device__ __forceinline__ void cluster_reduce_allreduce(const GemmParams& p, ui
     if (tid == 0) p.epoch[fidx] = cnt + 1u;
 }
 
-__global__ void __launch_bounds__(kGemmThreads, 1)
+// PERSIST = false: one CTA per (tile, K range), the K ranges of a tile in one
+// thread-block cluster (above). PERSIST = true (no K split, shapes with more
+// tiles than SMs): one CTA per SM loops over tiles blockIdx.x, + gridDim.x, ...;
+// its units are the K blocks of those tiles in order, so the producers and
+// decoders run on across tile boundaries; the MMA alternates between two TMEM
+// accumulators, and four more warps (one per TMEM lane quarter) drain each
+// finished tile to C while the next tile is decoded.
+constexpr int kEpiWarp0 = kDecWarps + 4;   // persistent mode: epilogue warps kEpiWarp0 .. + 3
+template <bool PERSIST>
+__global__ void __launch_bounds__(kGemmThreads + (PERSIST ? 128 : 0), 1)
     zipgemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     GemmHeader* hd = reinterpret_cast<GemmHeader*>(smem);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    // this CTA: output tile T, cluster rank r, K blocks [kb0, kb0 + n)
-    const int r = (int)(blockIdx.x % (unsigned)p.S);
-    const int T = (int)(blockIdx.x / (unsigned)p.S);
-    const int kb0 = (int)((long long)p.gtk * r / p.S);
-    const int n = (int)((long long)p.gtk * (r + 1) / p.S) - kb0;
-    const int nsub = (2 * T + 1 < p.mgt) ? 2 : 1;   // GT rows of this tile
+    // this CTA: first output tile T, cluster rank r, K blocks [kb0, kb0 + per)
+    // of each of its ntile tiles; n units in all
+    const int r = PERSIST ? 0 : (int)(blockIdx.x % (unsigned)p.S);
+    const int T = PERSIST ? (int)blockIdx.x : (int)(blockIdx.x / (unsigned)p.S);
+    const int kb0 = PERSIST ? 0 : (int)((long long)p.gtk * r / p.S);
+    const int per = PERSIST ? p.gtk : (int)((long long)p.gtk * (r + 1) / p.S) - kb0;
+    const int ntile = PERSIST ? (p.tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 1;
+    const int n = per * ntile;
+    auto tile_of = [&](int jt) { return PERSIST ? T + jt * (int)gridDim.x : T; };
+    auto nsub_of = [&](int t) { return (2 * t + 1 < p.mgt) ? 2 : 1; };
+    const int rowlen = p.nmax + 1;   // staged offsets: [ntile][2 GT rows][nmax + 1]
 
     if (tid == 0) ZS_STAMP(0);
-    int2* offs = reinterpret_cast<int2*>(smem + p.off_offs);   // [2][nmax + 1]
+    int2* offs = reinterpret_cast<int2*>(smem + p.off_offs);
     if (warp == kStreamWarp) {
-        // Stage the GT offsets of the CTA's unit boundaries 0..n of both GT rows
-        // (asynchronous copies, in flight during the set-up below).
-        for (int idx = lane; idx < 2 * (n + 1); idx += 32) {
-            const int row = idx / (n + 1), b = idx - row * (n + 1);
-            if (row < nsub)
-                cp_async8(offs + row * (p.nmax + 1) + b, p.gt_off + 2 * ((long long)(2 * T + row) * p.gtk + kb0 + b));
+        // Stage the GT offsets of the CTA's unit boundaries 0..per of both GT rows
+        // of each of its tiles (asynchronous copies, in flight during the set-up below).
+        for (int idx = lane; idx < ntile * 2 * (per + 1); idx += 32) {
+            const int jt = idx / (2 * (per + 1)), rem = idx - jt * 2 * (per + 1);
+            const int row = rem / (per + 1), b = rem - row * (per + 1);
+            const int t = tile_of(jt);
+            int2* dst = offs + (jt * 2 + row) * rowlen + b;
+            if (row < nsub_of(t))
+                cp_async8(dst, p.gt_off + 2 * ((long long)(2 * t + row) * p.gtk + kb0 + b));
             else
-                offs[row * (p.nmax + 1) + b] = make_int2(0, 0);
+                *dst = make_int2(0, 0);
         }
     }
     if (warp == kBmWarp) {
@@ -366,6 +385,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane < p.nb) { mbar_init(&hd->b_full[lane], 1); mbar_init(&hd->b_empty[lane], 1); }
         if (lane == 0) {
             mbar_init(&hd->acc_full, 1);
+            if (PERSIST) {
+                mbar_init(&hd->acc_full_p[0], 1);
+                mbar_init(&hd->acc_full_p[1], 1);
+                mbar_init(&hd->acc_empty_p[0], 4);
+                mbar_init(&hd->acc_empty_p[1], 4);
+            }
             prefetch_tmap(&maps.x);
             if ((smem_u32(smem) & 1023u) && p.err) atomicOr(p.err, kErrStreamOverflow);
         }
@@ -398,14 +423,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!bmw) cp_async_wait_all();
         __syncwarp();   // staged offsets visible to the whole warp (and, via the arrives below, to the decoders)
         const int crow = lane & 1;
-        const int2* orow0 = offs;
-        const int2* orow1 = offs + (p.nmax + 1);
         const CUtensorMap* tmap = lane == 0 ? &maps.b1 : lane == 1 ? &maps.b2 : lane == 2 ? &maps.b3 : &maps.mt;
         const uint64_t* plane = lane < 2 ? p.b1 : lane < 4 ? p.b2 : p.b3;
         int s = 0;
         uint32_t ph = 0;
         for (int c = 0, i0 = 0; i0 < n; ++c, i0 += p.cu) {
-            const int len = min(p.cu, n - i0);
+            // the chunk's tile (index jt of this CTA's tiles) and its first unit il in it;
+            // chunks never cross a tile (per is a multiple of cu in persistent mode)
+            const int jt = PERSIST ? i0 / per : 0, il = i0 - jt * per;
+            const int tt = tile_of(jt), ns = nsub_of(tt);
+            const int len = min(p.cu, per - il);
+            const int2* orow0 = offs + (jt * 2) * rowlen;
+            const int2* orow1 = orow0 + rowlen;
             if (bmw && c < 8 && lane == 0) ZS_CLK(128 + 4 * c);
             if (c >= p.nc) {
                 bool ok = true;
@@ -423,16 +452,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
 #endif
             if (bmw) {
-                const bool tiled = len == p.cu && nsub == 2;
-                if (lane == 0) mbar_arrive_expect_tx(full_bar, (3u * 512u + 32u) * (uint32_t)(len * nsub));
+                const bool tiled = len == p.cu && ns == 2;
+                if (lane == 0) mbar_arrive_expect_tx(full_bar, (3u * 512u + 32u) * (uint32_t)(len * ns));
                 __syncwarp();
                 if (bmw && c < 8 && lane == 0) ZS_CLK(129 + 4 * c);
                 if (tiled) {
                     if (lane < 4)
                         tma_load_2d(slot + (lane < 3 ? 1024u * (uint32_t)(lane * p.cu) : p.c_mt), tmap,
-                                    (kb0 + i0) * (lane < 3 ? 64 : 8), 2 * T, full_bar);
-                } else if (lane < 8 && crow < nsub) {
-                    const long long g = (long long)(2 * T + crow) * p.gtk + kb0 + i0;   // first GT of the chunk
+                                    (kb0 + il) * (lane < 3 ? 64 : 8), 2 * tt, full_bar);
+                } else if (lane < 8 && crow < ns) {
+                    const long long g = (long long)(2 * tt + crow) * p.gtk + kb0 + il;   // first GT of the chunk
                     if (lane < 6)
                         bulk_g2s(slot + 512u * (uint32_t)(((lane >> 1) * 2 + crow) * p.cu), plane + 64 * g,
                                  512u * (uint32_t)len, full_bar);
@@ -444,7 +473,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // stream ranges of the chunk, validated against the slot: lane 0 sums all four
                 auto range = [&](int row, bool hf, uint32_t& bytes, int& b0) {
                     const int2* o = row ? orow1 : orow0;
-                    const int2 f = o[i0], e = o[i0 + len];
+                    const int2 f = o[il], e = o[il + len];
                     const int beg = hf ? f.x : f.y, end = hf ? e.x : e.y;
                     const uint32_t cap = hf ? p.hf_area : 2u * p.full_area;
                     const int al = hf ? 16 : 8;
@@ -455,7 +484,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         bytes = min(bytes, cap) & ~15u;
                         b0 = max(b0, 0) & ~(al - 1);
                     }
-                    if (row >= nsub) bytes = 0;
+                    if (row >= ns) bytes = 0;
                 };
                 uint32_t bytes = 0;
                 int b0 = 0;
@@ -496,7 +525,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
 #endif
                 mbar_arrive_expect_tx(&hd->b_full[s], (uint32_t)p.xrows * 128u);
-                tma_load_2d(smem + p.off_b + (size_t)s * p.b_slot, &maps.x, (kb0 + i) * kGT, 0, &hd->b_full[s]);
+                tma_load_2d(smem + p.off_b + (size_t)s * p.b_slot, &maps.x, (kb0 + (PERSIST ? i % per : i)) * kGT, 0,
+                            &hd->b_full[s]);
                 if (++s == p.nb) { s = 0; ph ^= 1u; }
             }
         }
@@ -509,20 +539,58 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int sa = 0, sb = 0;
             uint32_t pa = 0, pb = 0;
             for (int i = 0; i < n; ++i) {
+                // persistent mode: tile jt accumulates in TMEM half jt & 1, which the
+                // epilogue warps must have drained (tile jt - 2) before its first MMA
+                const int jt = PERSIST ? i / per : 0, il = i - jt * per;
+                if (PERSIST && il == 0 && jt >= 2 &&
+                    !mbar_wait(&hd->acc_empty_p[jt & 1], (uint32_t)(((jt >> 1) - 1) & 1), p.err, abort_flag))
+                    break;
+                const uint32_t acc = tmem_d + (PERSIST ? (uint32_t)(jt & 1) * (p.tmem_cols / 2) : 0u);
                 if (!mbar_wait2(&hd->a_full[sa], pa, &hd->b_full[sb], pb, p.err, abort_flag)) break;
                 tc_fence_after();
                 if (i < 32) ZS_CLK(160 + i);
-                umma_bf16_ss(tmem_d, da, db, idesc, i > 0 ? 1u : 0u);
-                umma_bf16_ss(tmem_d, da + 2, db + 2, idesc, 1u);
-                umma_bf16_ss(tmem_d, da + 4, db + 4, idesc, 1u);
-                umma_bf16_ss(tmem_d, da + 6, db + 6, idesc, 1u);
+                umma_bf16_ss(acc, da, db, idesc, il > 0 ? 1u : 0u);
+                umma_bf16_ss(acc, da + 2, db + 2, idesc, 1u);
+                umma_bf16_ss(acc, da + 4, db + 4, idesc, 1u);
+                umma_bf16_ss(acc, da + 6, db + 6, idesc, 1u);
                 umma_commit(&hd->a_empty[sa]);
                 umma_commit(&hd->b_empty[sb]);
+                if (PERSIST && il == per - 1) umma_commit(&hd->acc_full_p[jt & 1]);
                 if (++sa == p.na) { sa = 0; pa ^= 1u; da = da0; } else { da += kATileBytes >> 4; }
                 if (++sb == p.nb) { sb = 0; pb ^= 1u; db = db0; } else { db += bstep; }
             }
-            umma_commit(&hd->acc_full);
+            if (!PERSIST) umma_commit(&hd->acc_full);
             ZS_STAMP(2);
+        }
+    } else if (PERSIST && warp >= kEpiWarp0) {
+        // ------------------- epilogue warps (persistent mode) -------------------
+        // warp kEpiWarp0 + q reads TMEM lane quarter q (rows 32 q .. 32 q + 31) of
+        // each finished tile, writes bf16 C and frees the accumulator half
+        const int q = warp & 3;
+        for (int jt = 0; jt < ntile; ++jt) {
+            if (!mbar_wait_sleep(&hd->acc_full_p[jt & 1], (uint32_t)((jt >> 1) & 1), p.err, abort_flag)) break;
+            tc_fence_after();
+            if (jt == 0) grid_dep_wait();   // C may still be in use by the previous grid
+            const int m = 128 * tile_of(jt) + 32 * q + lane;
+            const uint32_t acc = tmem_d + ((uint32_t)(32 * q) << 16) + (uint32_t)(jt & 1) * (p.tmem_cols / 2);
+            for (int c16 = 0; c16 < p.BN; c16 += 16) {
+                uint32_t v[16];
+                tmem_ld16(acc + (uint32_t)c16, v);
+                tmem_wait_ld();
+                if (m < p.M) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int nn = c16 + j;
+                        if (nn < p.N) {
+                            const __nv_bfloat16 b = __float2bfloat16_rn(__uint_as_float(v[j]));
+                            p.C[(size_t)nn * p.M + m] = *reinterpret_cast<const uint16_t*>(&b);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&hd->acc_empty_p[jt & 1]);
         }
     } else {
         // ------------------------------ decoders ------------------------------
@@ -548,11 +616,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (!ok) break;
             if (warp == 0 && u == 0 && lane == 0) ZS_STAMP(3);
             if ((warp & 3) == 0 && u < 32 && lane == 0) ZS_CLK(192 + u);
-            if (sub < nsub) {
+            const int jt = PERSIST ? u / per : 0, ul = u - jt * per;   // the unit's tile, K block in it
+            if (sub < nsub_of(tile_of(jt))) {
                 const uint32_t base = launder(smem0 + p.off_c + (uint32_t)cs * p.c_slot);
                 // the unit's stream starts inside its chunk, from the staged GT offsets
-                const int2* orow = offs + sub * (p.nmax + 1);
-                const int2 ou = orow[u], oc = orow[u - pos];
+                const int2* orow = offs + (jt * 2 + sub) * rowlen;
+                const int2 ou = orow[ul], oc = orow[ul - pos];
                 const uint32_t h0 = min((uint32_t)max(ou.x - oc.x, 0), p.hf_area);
                 const uint32_t f0 = min((uint32_t)max(ou.y - oc.y, 0), p.full_area);
                 const uint32_t su = (uint32_t)(sub * p.cu + pos);
@@ -587,7 +656,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             while (sa >= p.na) { sa -= p.na; ++around; }
         }
         // drain: warp w reads TMEM lane quarter w % 4 (rows 32 q .. 32 q + 31), columns 16 j + 16 (w / 4) ..
-        if (!*abort_flag && mbar_wait_sleep(&hd->acc_full, 0u, p.err, abort_flag)) {
+        if (!PERSIST && !*abort_flag && mbar_wait_sleep(&hd->acc_full, 0u, p.err, abort_flag)) {
             if (warp == 0 && lane == 0) ZS_STAMP(4);
             tc_fence_after();
             if (p.S == 1) grid_dep_wait();   // C may still be in use by the previous grid
@@ -685,8 +754,11 @@ static cudaError_t dev_setup(int dev, DevInfo* out) {
     if (!d.ready) {
         ZS_RETURN_IF_ERR(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
         ZS_RETURN_IF_ERR(cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-        ZS_RETURN_IF_ERR(cudaFuncSetAttribute(zipgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem));
-        ZS_RETURN_IF_ERR(cudaFuncSetAttribute(zipgemm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+        ZS_RETURN_IF_ERR(
+            cudaFuncSetAttribute(zipgemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem));
+        ZS_RETURN_IF_ERR(cudaFuncSetAttribute(zipgemm_kernel<false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+        ZS_RETURN_IF_ERR(
+            cudaFuncSetAttribute(zipgemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem));
         for (int i = 0; i < 4; ++i) {
             const int S = 1 << i;
             cudaLaunchConfig_t cfg = {};
@@ -701,7 +773,7 @@ static cudaError_t dev_setup(int dev, DevInfo* out) {
             cfg.attrs = attr;
             cfg.numAttrs = 1;
             int nclusters = 0;
-            if (cudaOccupancyMaxActiveClusters(&nclusters, zipgemm_kernel, &cfg) != cudaSuccess) {
+            if (cudaOccupancyMaxActiveClusters(&nclusters, zipgemm_kernel<false>, &cfg) != cudaSuccess) {
                 (void)cudaGetLastError();
                 nclusters = 0;
             }
@@ -730,6 +802,32 @@ static int choose_split(const DevInfo& di, long long tiles, int gtk, int min_s =
     return best;
 }
 
+// Persistent mode (one CTA per SM looping over its tiles, no K split) for
+// shapes with more tiles than SMs: chosen when its critical path, the units of
+// its busiest CTA plus one set-up and epilogue (about 8 units' time), is
+// shorter than the clustered launch's, which pays the set-up and epilogue once
+// per wave. ZS_ZIPGEMM_PERSIST=0 / 1 in the environment forces either mode
+// where both apply (for tests and comparisons).
+static bool choose_persistent(const DevInfo& di, long long tiles, int gtk, int S, int BN) {
+    constexpr double kWaveOverheadUnits = 8.0;
+    const int G = di.sms;
+    const long long ntm = (tiles + G - 1) / G;
+    int half = 32;
+    while (half < BN) half <<= 1;
+    if (tiles < 2 || 2 * half > 512 || ntm * 2 * (gtk + 1) * 8 > 16384) return false;
+    if (const char* e = getenv("ZS_ZIPGEMM_PERSIST")) {
+        if (e[0] == '0') return false;
+        if (e[0] == '1') return true;
+    }
+    int li = 0;
+    while ((1 << li) < S) ++li;
+    if (di.clusters[li] <= 0) return true;
+    const double np_cost = (double)((tiles + di.clusters[li] - 1) / di.clusters[li]) *
+                           ((double)((gtk + S - 1) / S) + kWaveOverheadUnits);
+    const double p_cost = (double)ntm * (double)gtk + kWaveOverheadUnits;
+    return p_cost < np_cost;
+}
+
 static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, GemmParams p, const uint16_t* X,
                                 int max_hf, int max_full) {
     auto encode = get_encode_fn();
@@ -752,6 +850,14 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, GemmPara
     }
     p.tmem_cols = 32;
     while (p.tmem_cols < (uint32_t)p.BN) p.tmem_cols <<= 1;
+    p.tiles = (int)tiles;
+    const bool persist = p.world == 1 && choose_persistent(di, tiles, p.gtk, p.S, p.BN);
+    long long ntm = 1;   // most tiles of any CTA
+    if (persist) {
+        p.S = 1;
+        p.tmem_cols *= 2;   // two accumulators
+        ntm = (tiles + di.sms - 1) / di.sms;
+    }
 
     // Shared memory: header | staged GT offsets | A ring | X ring | compressed ring. The compressed ring takes chunks of cu units (the
     // decoders check each slot's chunk tag before its parity, so any depth is
@@ -773,7 +879,7 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, GemmPara
     };
     p.nmax = (p.gtk + p.S - 1) / p.S;
     p.off_offs = kHeaderBytes;
-    const uint32_t ring0 = round_up_u32(kHeaderBytes + 16u * (uint32_t)(p.nmax + 1), 1024);
+    const uint32_t ring0 = round_up_u32(kHeaderBytes + 16u * (uint32_t)ntm * (uint32_t)(p.nmax + 1), 1024);
     auto fits = [&](int na, int nb, int nc) {
         return ring0 + (uint32_t)na * kATileBytes + (uint32_t)nb * p.b_slot + (uint32_t)nc * p.c_slot <= budget;
     };
@@ -786,6 +892,7 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, GemmPara
     bool placed = false;
     for (const Cfg& q : prefs) {
         if (q.cu > p.gtk) continue;   // a tensor box spans cu K blocks of one GT row
+        if (persist && p.gtk % q.cu) continue;   // chunks must not cross a tile
         layout(q.cu);
         if (q.na <= kMaxRing && fits(q.na, q.nb, q.nc)) { p.nc = q.nc; p.na = q.na; p.nb = q.nb; placed = true; break; }
     }
@@ -834,8 +941,8 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, GemmPara
         return cudaErrorInvalidValue;
 
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(tiles * p.S), 1, 1);
-    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.gridDim = dim3((unsigned)(persist ? std::min<long long>(tiles, di.sms) : tiles * p.S), 1, 1);
+    cfg.blockDim = dim3(kGemmThreads + (persist ? 128 : 0), 1, 1);
     cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -850,7 +957,8 @@ static cudaError_t launch_chunk(cudaStream_t stream, const DevInfo& di, GemmPara
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, zipgemm_kernel, maps, p);
+    return persist ? cudaLaunchKernelEx(&cfg, zipgemm_kernel<true>, maps, p)
+                   : cudaLaunchKernelEx(&cfg, zipgemm_kernel<false>, maps, p);
 }
 
 static cudaError_t zipgemm_impl(cudaStream_t stream, const uint8_t* sm, const uint16_t* full, const uint64_t* b1,
