@@ -442,6 +442,14 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
     return d;
 }
 
+// Bytes c & 3 .. (c & 3) + 3 of the 8-byte value {b, a} (a low): a funnel
+// shift right by 8 (c & 3) bits that takes the byte offset itself.
+__device__ __forceinline__ uint32_t prmt_f4e(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("prmt.b32.f4e %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 __device__ __forceinline__ uint32_t lop_or_and(uint32_t a, uint32_t mask, uint32_t b) {
     return (a & mask) | b;  // compiles to a single LOP3
 }
@@ -483,10 +491,9 @@ __device__ __forceinline__ void decode_row_words(const RowGroups& g, uint32_t r,
     const uint32_t X = s1 + (s2 << 1) + (s3 << 2);        // code nibbles
     const uint32_t sel = (s1 | s2 | s3) * 0x11111110u;    // hf-before-j nibbles
     const uint32_t wa = win & ~3u;
-    const uint32_t sh = (win & 3u) * 8u;
     const uint32_t q0 = lds32(wa), q1 = lds32(wa + 4), q2 = lds32(wa + 8);
-    const uint32_t lo = __funnelshift_r(q0, q1, sh);
-    const uint32_t hi = __funnelshift_r(q1, q2, sh);
+    const uint32_t lo = prmt_f4e(q0, q1, win);   // the 8 bytes from `win` on
+    const uint32_t hi = prmt_f4e(q1, q2, win);
     const uint32_t s_lo = prmt(lo, hi, sel);
     const uint32_t s_hi = prmt(lo, hi, sel >> 16);
     const uint32_t hb_lo = lop_or_and(s_lo, 0x80808080u, prmt(t.thb0, t.thb1, X));
