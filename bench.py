@@ -689,11 +689,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world == 1 and not args.headline_only:
         # the other BASELINE configurations, one JSON line per case, before the headline
-        import torch as _t
         for run in (run_roundtrip, run_llama8b, run_attention):
             run(args)
-            _t.cuda.synchronize()
-            _t.cuda.empty_cache()
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
