@@ -575,6 +575,7 @@ def tp70b_lines(world, rank, dev, reps=20):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out.append({"workload": "config4_tp70b_layer", "tp": world, "N": N, "layer_us": round(t.item(), 2),
                     "per_rank_compressed_MB": round(cb / 1e6, 2), "per_rank_GBps": round(cb / t.item() / 1e3, 1),
+                    "hbm_frac": round(cb / t.item() / 1e3 / peaks()[0], 4),
                     "compress_layer_ms": round(comp_ms, 2),
                     "compress_GBps_bf16_in": round(in_bytes / comp_ms / 1e6, 1),
                     "note": "4 projections per layer" + (
@@ -615,7 +616,24 @@ def compress80_line(world, rank, dev, layers=80):
     t = torch.tensor([total_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    cpu = None
+    if rank == 0:
+        # CPU baseline (bounded sample): the library's host encoder (OpenMP, all
+        # cores; the reference's host encoders produce the same bytes) on one O
+        # shard, extrapolated by bf16 bytes to the rank's 80 layers
+        from zipserv_asplos26_b200.codec import compress_host
+        ko = LLAMA70B_SHAPES["o"][1] // world
+        w = (torch.randn(LLAMA70B_SHAPES["o"][0], ko, generator=torch.Generator().manual_seed(3)) * 0.02).to(
+            torch.bfloat16)
+        compress_host(w)
+        t0 = time.perf_counter()
+        compress_host(w)
+        dt = time.perf_counter() - t0
+        cpu = {"seconds_extrapolated": round(dt * in_bytes / (2 * w.numel()), 2), "cores": os.cpu_count() or 1,
+               "kind": "port", "sample": f"host encode of one {LLAMA70B_SHAPES['o'][0]}x{ko} O shard "
+                                         f"({round(dt * 1e3, 1)} ms), scaled by bytes to {layers} layers"}
     return {"workload": "config4_whole_model_compression", "tp": world, "layers": layers,
+            "cpu_baseline": cpu,
             "seconds": round(t.item() / 1e3, 4), "per_rank_bf16_GB": round(in_bytes / 1e9, 2),
             "per_rank_compressed_GB": round(out_bytes / 1e9, 2), "ratio": round(in_bytes / out_bytes, 4),
             "GBps_bf16_in": round(in_bytes / (t.item() / 1e3) / 1e9, 1),
