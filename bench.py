@@ -258,6 +258,14 @@ def _graph_time_us(torch, fns, stream, reps=3):
     return best
 
 
+_LINES = []   # the per-case lines printed so far (summarised in the headline line)
+
+
+def _emit(line):
+    print(json.dumps(line), flush=True)
+    _LINES.append(line)
+
+
 def run_llama8b(args):
     """Config 3: Llama-3.1-8B projection shapes, N in {1..256}; W ~ N(0, sigma),
     sigma ~ U[0.01, 0.04] per matrix; compared with dense bf16 torch.matmul (cuBLAS)."""
@@ -293,12 +301,12 @@ def run_llama8b(args):
             cb = comps[0].compressed_bytes()
             nbytes = cb + 2 * N * K + 2 * M * N
             gbps = nbytes / tz / 1e3
-            print(json.dumps({"workload": "config3_llama8b", "proj": name, "M": M, "K": K, "N": N, "sigma": round(sigma, 4),
+            _emit({"workload": "config3_llama8b", "proj": name, "M": M, "K": K, "N": N, "sigma": round(sigma, 4),
                               "zipgemm_us": round(tz, 2), "dense_bf16_us": round(td, 2), "speedup_vs_dense": round(td / tz, 3),
                               "compressed_GBps": round(gbps, 1), "hbm_frac": round(gbps / peak, 4),
                               "tflops": round(2 * M * N * K / tz / 1e6, 2), "ratio": round(2 * M * K / cb, 4),
-                              "peak": f"{peak} GB/s ({kind})", "split_k": "stream-K (SplitK argument is a hint)"}),
-                  flush=True)
+                   "peak": f"{peak} GB/s ({kind})",
+                   "split_k": "the SplitK argument is accepted; the kernel picks its K split per shape"})
         del comps, dense
 
 
@@ -395,14 +403,14 @@ def run_attention(args):
                 del dsets
             except ImportError:
                 pass
-            print(json.dumps({"workload": "config5_decode_attention", "B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "D": D,
+            _emit({"workload": "config5_decode_attention", "B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "D": D,
                               "us": round(t, 2), "tok_per_s": round(B / (t * 1e-6), 1),
                               "dense_flash_attn_us": round(fa_us, 2) if fa_us else None,
                               "speedup_vs_dense_flash_attn": round(fa_us / t, 3) if fa_us else None,
                               "compressed_GBps": round(nbytes / t / 1e3, 1), "hbm_frac": round(nbytes / t / 1e3 / peak, 4),
                               "dense_equiv_GBps": round((dense + 4 * B * Hq * D) / t / 1e3, 1),
                               "kv_ratio": round(dense / cb, 4), "rotating_sets": nsets,
-                              "peak": f"{peak} GB/s ({kind})"}), flush=True)
+                   "peak": f"{peak} GB/s ({kind})"})
             del sets, kc, vc
             torch.cuda.empty_cache()
 
@@ -512,11 +520,11 @@ def run_roundtrip(args):
     t_genc = ev[0].elapsed_time(ev[1]) / 10 * 1e3
     t_gdec = _graph_time_us(torch, [lambda: zs.decompress(gc)] * 20, stream)
     cb = gc.compressed_bytes()
-    print(json.dumps({"workload": "config1_roundtrip", "M": M_, "K": K_, "ratio": round(2 * M_ * K_ / cb, 4),
+    _emit({"workload": "config1_roundtrip", "M": M_, "K": K_, "ratio": round(2 * M_ * K_ / cb, 4),
                       "compressed_bytes": cb, "host_encode_ms": round(t_enc * 1e3, 2), "host_cores": cores,
                       "gpu_encode_us": round(t_genc, 1), "gpu_decode_us": round(t_gdec, 2),
                       "gpu_decode_GBps": round((cb + 2 * M_ * K_) / t_gdec / 1e3, 1),
-                      "host_gpu_bytes_identical": bool(same), "round_trip_bit_exact": bool(exact)}), flush=True)
+                      "host_gpu_bytes_identical": bool(same), "round_trip_bit_exact": bool(exact)})
 
 
 def tp70b_lines(world, rank, dev, reps=20):
@@ -661,6 +669,27 @@ def run_tp70b(args):
         dist.barrier()
         sys.stdout.flush()
         os._exit(0)
+
+
+def _summarise(lines, layer_lines):
+    """Compact summary of the per-case lines printed before the headline, kept
+    in the headline line itself (the line a log reader parses)."""
+    out = {}
+    for d in lines:
+        w = d.get("workload")
+        if w == "config1_roundtrip":
+            out["config1_roundtrip"] = {k: d[k] for k in ("ratio", "host_encode_ms", "host_cores", "gpu_encode_us",
+                                                          "gpu_decode_us", "round_trip_bit_exact",
+                                                          "host_gpu_bytes_identical")}
+        elif w == "config3_llama8b":
+            out.setdefault("config3_llama8b_us_zipgemm_vs_cublas", {})[f"{d['proj']} N={d['N']}"] = [
+                d["zipgemm_us"], d["dense_bf16_us"]]
+        elif w == "config5_decode_attention":
+            out.setdefault("config5_attention_us_ours_vs_flash_attn_dense", {})[f"B={d['B']} T={d['T']}"] = [
+                d["us"], d["dense_flash_attn_us"]]
+    for d in layer_lines:
+        out.setdefault("config4_tp70b_layer_us", {})[f"tp={d['tp']} N={d['N']}"] = d["layer_us"]
+    return out
 
 
 def dense_bf16_us(torch, dev, steps=40):
@@ -933,6 +962,8 @@ def main():
             "gpu_launches": K,
             "clocks": clocks,
         }
+        if _LINES or layer_lines:
+            line["other_configs"] = _summarise(_LINES, layer_lines)
         if world == 1 and not args.no_cpu_baseline:
             v, per, cores, desc = cpu_step_sample()
             line["cpu_baseline"] = {"value": v / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
